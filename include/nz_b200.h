@@ -1,0 +1,224 @@
+/*
+ * nz_b200.h — C ABI of the B200-native NeuralZip decompression path.
+ *
+ * One shared library (libnzb200.so) exports every symbol declared here. All
+ * signatures use plain pointers, sizes and fixed-layout structs; no torch or
+ * Python types cross the boundary. Every entry point returns an int status
+ * (NZ_OK = 0); on failure a thread-local message is available through
+ * nz_last_error(). The status maps onto the exception classes the reference
+ * raises for the same conditions (neuralzip/native/common.h:59-63 `require<>`
+ * plus nanobind's translation): NZ_EVALUE -> ValueError, NZ_ETYPE ->
+ * TypeError, NZ_EOVERFLOW -> OverflowError, NZ_ERUNTIME -> RuntimeError.
+ *
+ * Layout produced by the packer and consumed by the decode kernel
+ * ("tile layout"): a group is one source chunk of one tensor's selected byte
+ * lane (neuralzip/gpu/inference.py:302-330). Its elements are cut into
+ * sub-streams of NZ_LANE_ELEMS consecutive elements; NZ_TILE_LANES
+ * sub-streams form one tile, decoded by one warp (one sub-stream per lane).
+ * Sub-streams are Huffman bitstreams packed back to back, MSB-first, stored
+ * as 32-bit words whose bit 31 is the earliest bit. `lens[s]` holds the bit
+ * length of sub-stream s and `tile_off[t]` the bit offset of tile t's first
+ * sub-stream; a lane finds its start with a warp scan of its tile's lens.
+ * A pair token never straddles two sub-streams. The non-selected byte lanes
+ * are stored raw, one byte per element, 16-byte aligned.
+ */
+#ifndef NZ_B200_H
+#define NZ_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define NZ_LANE_ELEMS 256u
+#define NZ_TILE_LANES 32u
+#define NZ_TILE_ELEMS (NZ_LANE_ELEMS * NZ_TILE_LANES)
+#define NZ_LUT_BITS 12u
+#define NZ_LUT_ENTRIES (1u << NZ_LUT_BITS)
+#define NZ_TREE_MAX_NODES 512u
+#define NZ_LUT_WORDS (NZ_LUT_ENTRIES + 2u * NZ_TREE_MAX_NODES)
+#define NZ_MAX_CODE_BITS 56u
+#define NZ_MAX_SINGLETON_BITS 12u
+#define NZ_MAX_PAIRS 254u
+#define NZ_BITS_PAD_WORDS 8u
+#define NZ_RAW_LUT 0xFFFFFFFFu
+
+enum nz_status {
+    NZ_OK = 0,
+    NZ_EVALUE = 1,
+    NZ_ETYPE = 2,
+    NZ_EOVERFLOW = 3,
+    NZ_ERUNTIME = 4,
+    NZ_ECUDA = 5
+};
+
+/* Byte-lane layout of one floating format; mirrors DTypeSpec
+ * (neuralzip/dtypes.py:8-50) and the packer arguments of encode_gpu_tensor
+ * (neuralzip/native/binding_helpers.h:125-195). */
+typedef struct nz_dtype {
+    uint32_t elem_size;  /* 2 or 4 */
+    uint32_t reorder;    /* 1: sign moved below the exponent (bf16, fp32) */
+    uint32_t mant_bits;  /* 7 bf16, 10 fp16, 23 fp32 */
+    uint32_t exp_bits;   /* 8 bf16/fp32, 5 fp16 */
+    uint32_t stream_id;  /* byte lane holding the Huffman-coded symbols */
+} nz_dtype;
+
+/* Opaque host codebook: canonical codes, pair lookup and decode table. */
+typedef struct nz_codebook nz_codebook;
+
+/* ---- host: codebooks -------------------------------------------------- */
+
+/* Replaces export_code_table (neuralzip/native/binding_helpers.h:103-123,
+ * module.cpp:57-62). `header` is either a mixed table ("NZM1" + 256..510
+ * code lengths, neuralzip/native/mixed_huffman.h:5-83) or a Huff0 table
+ * header (RFC 8878 section 4.2.1). Writes one length and one canonical
+ * code value per symbol (cap >= 256 + vocab_size / 2). */
+int nz_export_code_table(const uint8_t* header, size_t header_size,
+                         const uint8_t* vocab, size_t vocab_size,
+                         uint32_t max_bits, uint8_t* lengths_out,
+                         uint64_t* values_out, uint32_t cap,
+                         uint32_t* nsym_out, uint32_t* longest_out);
+
+/* Builds a codebook from explicit per-symbol code lengths and values (the
+ * GPUCodebook inputs, neuralzip/gpu/inference.py:20-27). `values` may be
+ * NULL, in which case canonical mixed-table codes are assigned
+ * (mixed_huffman.h:5-83 semantics). nsym = 256 + vocab_size / 2. */
+int nz_codebook_create(const uint8_t* lengths, const uint64_t* values,
+                       uint32_t nsym, const uint8_t* vocab,
+                       uint32_t vocab_size, nz_codebook** out);
+int nz_codebook_destroy(nz_codebook* codebook);
+/* Longest code length and the number of suffix-tree nodes. */
+int nz_codebook_info(const nz_codebook* codebook, uint32_t* longest,
+                     uint32_t* tree_nodes);
+/* Decode table of the tile kernel (replaces GPUCodebook.decode_lut,
+ * neuralzip/gpu/inference.py:28-75). Writes NZ_LUT_WORDS words. */
+int nz_codebook_lut(const nz_codebook* codebook, uint32_t* lut,
+                    uint32_t cap_words);
+
+/* Setup-time singleton tables (replaces build_codebook_from_counts ->
+ * HUF_buildCTable_wksp + HUF_writeCTable_wksp, neuralzip/native/
+ * codebooks.h:20-39, binding_helpers.h:68-90): Huffman code lengths limited
+ * to max_bits (<= 12) for a 256-bin histogram, serialized as an RFC 8878
+ * Huff0 header. lengths_out (256 bytes) may be NULL. */
+int nz_huff0_build(const uint64_t* counts, uint32_t max_bits, uint8_t* header_out,
+                   size_t cap, size_t* size_out, uint8_t* lengths_out);
+/* Reads a Huff0 header (replaces HUF_readCTable, codebooks.h:60-68):
+ * 256 code lengths, canonical values (may be NULL), table log and the
+ * number of header bytes consumed. */
+int nz_huff0_read(const uint8_t* header, size_t size, uint8_t* lengths_out,
+                  uint16_t* values_out, uint32_t* table_log, size_t* consumed);
+
+/* ---- host: packer ----------------------------------------------------- */
+
+/* Capacities for nz_pack_chunk: bitstream words (padding included),
+ * lens entries and tile count for `numel` elements whose longest code is
+ * `longest` bits. */
+int nz_pack_bound(uint64_t numel, uint32_t longest, uint64_t* bits_words,
+                  uint64_t* lens_count, uint64_t* tiles);
+
+/* Replaces encode_gpu_tensor / encode_gpu_layout
+ * (neuralzip/native/binding_helpers.h:125-195, gpu_layout.h:62-241).
+ * Splits `raw` (numel elements of dt->elem_size bytes) into byte lanes,
+ * writes the non-selected lanes to lanes[lane] (entries for the selected
+ * lane are ignored and may be NULL) and Huffman-codes the selected lane
+ * into the tile layout. Thread-safe; releases nothing it did not take. */
+int nz_pack_chunk(const nz_codebook* codebook, const uint8_t* raw,
+                  uint64_t numel, const nz_dtype* dt, uint32_t* bits,
+                  uint64_t bits_cap_words, uint16_t* lens,
+                  uint64_t lens_cap, uint32_t* tile_off, uint64_t tiles_cap,
+                  uint8_t* const* lanes, uint64_t* bit_length_out,
+                  uint64_t* words_used_out);
+
+/* Many chunks on a host thread pool (replaces the per-chunk Python loop of
+ * neuralzip/gpu/inference.py:308-330). Job i packs raws[i] with
+ * codebooks[i] into its own caller buffers; threads = 0 uses every core. */
+typedef struct nz_pack_job {
+    const nz_codebook* codebook;
+    const uint8_t* raw;
+    uint64_t numel;
+    uint32_t* bits;
+    uint64_t bits_cap_words;
+    uint16_t* lens;
+    uint64_t lens_cap;
+    uint32_t* tile_off;
+    uint64_t tiles_cap;
+    uint8_t* lanes[4];
+    uint64_t bit_length;  /* out */
+    uint64_t words_used;  /* out */
+    int32_t status;       /* out */
+    int32_t pad;
+} nz_pack_job;
+int nz_pack_many(nz_pack_job* jobs, uint64_t count, const nz_dtype* dt,
+                 int32_t threads);
+
+/* Raw fragment (no codebook, neuralzip/gpu/inference.py:319-324): applies
+ * the reorder and writes every byte lane, the selected one included. */
+int nz_split_lanes(const uint8_t* raw, uint64_t numel, const nz_dtype* dt,
+                   uint8_t* const* lanes);
+
+/* ---- device: decode --------------------------------------------------- */
+
+/* One group of a decode launch (device-resident array). Pointers are
+ * device addresses. lut == NZ_RAW_LUT marks a raw group whose selected
+ * lane is lanes[stream_id]. */
+typedef struct nz_group {
+    uint64_t bits;       /* const uint32_t*: tile-layout bitstream */
+    uint64_t lens;       /* const uint16_t*: bit length per sub-stream */
+    uint64_t tile_off;   /* const uint32_t*: bit offset per tile */
+    uint64_t lanes[4];   /* const uint8_t*: byte lanes by lane index */
+    uint64_t out;        /* element words */
+    uint32_t numel;
+    uint32_t lut;
+} nz_group;
+
+/* One tile of work: (group index, tile index within the group). */
+typedef struct nz_work {
+    uint32_t group;
+    uint32_t tile;
+} nz_work;
+
+/* One CTA: a contiguous range of works sharing one decode table. */
+typedef struct nz_cta {
+    uint32_t lut;        /* index into luts, or NZ_RAW_LUT */
+    uint32_t begin;
+    uint32_t end;
+    uint32_t lut_words;  /* words of the table to stage (<= NZ_LUT_WORDS) */
+} nz_cta;
+
+/* Replaces CuPyDecoder.decode_batch (neuralzip/gpu/decoder.py:193-208) and
+ * the kernel launch of decode_batched (neuralzip/gpu/cuda/decode.cu:323).
+ * All arrays are device-resident; `luts` is a device array of device
+ * pointers to NZ_LUT_WORDS-word tables. `status` (device int32) receives a
+ * nonzero code if a corrupt table made a lane give up; it is only written
+ * on error. Asynchronous on `cuda_stream` (a cudaStream_t, NULL = legacy
+ * default stream). warps_per_cta: 1..32 (0 = default). */
+typedef struct nz_launch {
+    nz_dtype dtype;
+    uint32_t warps_per_cta;
+    uint64_t groups;  /* const nz_group* */
+    uint64_t works;   /* const nz_work* */
+    uint64_t ctas;    /* const nz_cta* */
+    uint64_t luts;    /* const uint64_t* */
+    uint64_t status;  /* int32_t* */
+    uint32_t n_ctas;
+    uint32_t pad;
+} nz_launch;
+int nz_decode_launch(const nz_launch* launch, void* cuda_stream);
+
+/* Dynamic shared memory one CTA of nz_decode_launch uses. */
+int nz_decode_smem_bytes(uint32_t warps_per_cta, uint32_t* bytes);
+
+/* ---- errors ------------------------------------------------------------ */
+
+/* Copies the calling thread's last error message (NUL-terminated). */
+int nz_last_error(char* buf, size_t cap);
+/* ABI version of this header, for loaders. */
+int nz_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NZ_B200_H */

@@ -1,0 +1,208 @@
+"""GPU decoder host: prepares tile-decode launches and enqueues them.
+
+Same protocol as neuralzip/gpu/decoder.py (CuPyDecoder): ``default_decoder()``
+returns a process-wide decoder with ``prepare_group(device_index, group)``,
+``prepare_batch(groups) -> PreparedBatch`` and ``decode_batch(prepared)``,
+which launches on the torch current stream and returns the outputs
+(decoder.py:121-208). ``_DECODER`` may be replaced (tests do), and
+``shared_memory_bytes`` / ``KERNEL_PATH`` exist as in the reference.
+
+What differs is the device side. There is no NVRTC compilation: the sm_100a
+kernel is prebuilt in libnzb200.so and reached through the C ABI
+(``nz_decode_launch``). One launch covers every group of one dtype,
+whatever its codebook (singleton, mixed, long codes, raw), so a block needs
+one launch per dtype instead of one per (layout, staging) combination. The
+launch geometry is a list of (group, tile) works cut into CTAs that share a
+decode table; ``staging_policy`` (warps per CTA, works per CTA) can be
+overridden the way the reference's tests override ``_staging``.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass, field
+from pathlib import Path
+
+import numpy as np
+import torch
+
+from neuralzip_b200 import _native
+
+KERNEL_PATH = Path(__file__).resolve().parent.parent / "csrc" / "nz_decode.cu"
+WARPS_PER_CTA = 8
+SM_COUNT_DEFAULT = 148
+
+
+def shared_memory_bytes(warps_per_cta=WARPS_PER_CTA, max_elements=None):
+    """Dynamic shared memory of one decode CTA (decode table + warp staging).
+
+    ``max_elements`` is accepted for signature compatibility with the
+    reference (decoder.py:53-54); the tile kernel's footprint does not grow
+    with the group size."""
+    del max_elements
+    return _native.decode_smem_bytes(warps_per_cta)
+
+
+def _native_dtype(spec):
+    return _native.dtype_struct(spec.element_size, spec.bit_reorder, spec.mantissa_bits,
+                                spec.exponent_bits, spec.gpu_stream)
+
+
+@dataclass(frozen=True)
+class DeviceGroup:
+    """Device addresses of one uploaded group (what a launch descriptor needs)."""
+
+    spec: object            # DTypeSpec
+    numel: int
+    lut_index: int          # row in the decode-table tensor, or _native.RAW_LUT
+    lut_ptr: int            # device address of that row (0 for raw)
+    lut_words: int
+    bits: int
+    lens: int
+    tile_off: int
+    lanes: tuple            # 4 device addresses (0 where unused)
+    out: int
+    output: torch.Tensor = field(repr=False, compare=False)
+
+    @property
+    def tiles(self):
+        return (self.numel + _native.TILE_ELEMS - 1) // _native.TILE_ELEMS
+
+
+@dataclass(frozen=True)
+class PreparedBatch:
+    descriptor_tensors: tuple = field(repr=False)
+    device: torch.device
+    layout: tuple
+    warps_per_cta: int
+    shared_memory: int
+    kernel_grid: tuple
+    launch: object = field(repr=False)
+    outputs: tuple = field(repr=False)
+    status: torch.Tensor = field(repr=False)
+    works: int = 0
+    elements: int = 0
+
+
+class TileDecoder:
+    """Host side of the sm_100a tile decode kernel."""
+
+    def __init__(self):
+        self._sm_count = {}
+
+    # Reference hook: the staging policy decides the launch geometry.
+    def staging_policy(self, device_index, total_works):
+        """(warps per CTA, works per CTA) for a launch of `total_works` tiles."""
+        sms = self._sms(device_index)
+        nw = WARPS_PER_CTA
+        resident = 4 * sms
+        k = max(1, min(4, total_works // max(1, resident * nw)))
+        return nw, nw * k
+
+    def _sms(self, device_index):
+        if device_index not in self._sm_count:
+            try:
+                self._sm_count[device_index] = torch.cuda.get_device_properties(device_index).multi_processor_count
+            except (RuntimeError, AssertionError):
+                self._sm_count[device_index] = SM_COUNT_DEFAULT
+        return self._sm_count[device_index]
+
+    def prepare_group(self, device_index, group):
+        """Validates a GPUWeightGroup before any weight is removed
+        (neuralzip/gpu/decoder.py:121-128): the dtype must have a tile
+        kernel and the codebook a decode table."""
+        spec = group.encoded.dtype
+        _native.load()
+        key = (spec.element_size, bool(spec.bit_reorder), spec.mantissa_bits, spec.exponent_bits,
+               spec.gpu_stream)
+        if key not in {(2, True, 7, 8, 1), (2, False, 10, 5, 1), (4, True, 23, 8, 3)}:
+            raise ValueError("The GPU decoder has no kernel for this dtype layout.")
+        if group.codebook.max_bits and group.codebook.decode_lut is None:
+            raise ValueError("The GPU codebook has no decode table.")
+        return shared_memory_bytes()
+
+    def prepare_batch(self, groups):
+        """Builds the device descriptors of one launch over DeviceGroups of
+        one dtype (neuralzip/gpu/decoder.py:130-191)."""
+        groups = tuple(groups)
+        if not groups:
+            raise ValueError("A decode batch must contain at least one group.")
+        device = groups[0].output.device
+        if device.type != "cuda" or any(g.output.device != device for g in groups):
+            raise ValueError("A decode batch must use one CUDA device.")
+        spec = groups[0].spec
+        if any(g.spec != spec for g in groups):
+            raise ValueError("A decode batch must use one layout.")
+        table = np.zeros(len(groups), dtype=_native.GROUP_DTYPE)
+        for i, g in enumerate(groups):
+            table[i] = (g.bits, g.lens, g.tile_off, g.lanes, g.out, g.numel, g.lut_index)
+        # Works sorted by decode table so each CTA stages one table.
+        lut_ids = sorted({g.lut_index for g in groups})
+        lut_slot = {lut: i for i, lut in enumerate(lut_ids)}
+        lut_ptrs = np.array([next(g.lut_ptr for g in groups if g.lut_index == lut) for lut in lut_ids],
+                            dtype=np.uint64)
+        lut_words = {g.lut_index: g.lut_words for g in groups}
+        for i, g in enumerate(groups):
+            table[i]["lut"] = _native.RAW_LUT if g.lut_index == _native.RAW_LUT else lut_slot[g.lut_index]
+        order = sorted(range(len(groups)), key=lambda i: (groups[i].lut_index, i))
+        total_works = sum(groups[i].tiles for i in order)
+        nw, per_cta = self.staging_policy(device.index, total_works)
+        works = np.zeros(total_works, dtype=_native.WORK_DTYPE)
+        ctas = []
+        cursor = 0
+        for lut in lut_ids:
+            begin = cursor
+            for i in order:
+                if groups[i].lut_index != lut:
+                    continue
+                n = groups[i].tiles
+                works["group"][cursor:cursor + n] = i
+                works["tile"][cursor:cursor + n] = np.arange(n, dtype=np.uint32)
+                cursor += n
+            slot = _native.RAW_LUT if lut == _native.RAW_LUT else lut_slot[lut]
+            words = 0 if lut == _native.RAW_LUT else lut_words[lut]
+            for start in range(begin, cursor, per_cta):
+                ctas.append((slot, start, min(cursor, start + per_cta), words))
+        cta_array = np.array(ctas, dtype=_native.CTA_DTYPE)
+        if not len(lut_ptrs):
+            lut_ptrs = np.zeros(1, dtype=np.uint64)
+        tensors = tuple(
+            torch.from_numpy(a.view(np.uint8).copy()).to(device)
+            for a in (table, works, cta_array, lut_ptrs)
+        )
+        status = torch.zeros(1, dtype=torch.int32, device=device)
+        launch = _native.Launch()
+        launch.dtype = _native_dtype(spec)
+        launch.warps_per_cta = nw
+        launch.groups, launch.works, launch.ctas, launch.luts = (t.data_ptr() for t in tensors)
+        launch.status = status.data_ptr()
+        launch.n_ctas = len(cta_array)
+        layout = (spec.element_size, bool(spec.bit_reorder), spec.mantissa_bits, spec.exponent_bits,
+                  spec.gpu_stream)
+        return PreparedBatch(
+            descriptor_tensors=tensors, device=device, layout=layout, warps_per_cta=nw,
+            shared_memory=shared_memory_bytes(nw), kernel_grid=(len(cta_array),), launch=launch,
+            outputs=tuple(g.output for g in groups), status=status, works=total_works,
+            elements=sum(g.numel for g in groups),
+        )
+
+    def decode_batch(self, prepared, stream=None):
+        """Enqueues the decode on `stream` (default: torch's current stream)."""
+        if stream is None:
+            stream = torch.cuda.current_stream(device=prepared.device)
+        _native.decode_launch(prepared.launch, stream.cuda_stream)
+        return prepared.outputs
+
+    @staticmethod
+    def check_status(prepared):
+        """Raises if a launch of this batch reported a corrupt decode table."""
+        code = int(prepared.status.item())
+        if code:
+            raise RuntimeError(f"The GPU decoder reported status {code} (corrupt decode table).")
+
+
+_DECODER = TileDecoder()
+
+
+def default_decoder():
+    return _DECODER

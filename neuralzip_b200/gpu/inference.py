@@ -1,0 +1,547 @@
+"""Compressed GPU representation and the per-block runtime.
+
+Mirrors the public surface of neuralzip/gpu/inference.py: ``GPUCodebook``,
+``GPUEncodedSymbols``, ``GPUEncoded``, ``encode_gpu_native``,
+``LinearWeightBinding``, ``GPUWeightGroup``, ``NeuralZipModelExport``,
+``export_model_for_gpu`` and ``NeuralZipRuntime`` (attach, workspaces,
+``_decode_block``, ``materialized_weights``), with the same semantics for
+candidate discovery (inference.py:219-285), chunk grouping (one group per
+source chunk, raw fragments included, a tensor skipped when its fragments are
+not smaller than raw, inference.py:288-336) and weight binding.
+
+The encoded form is the tile layout of include/nz_b200.h rather than the
+reference's segment/gap layout (the GPU layout is an in-memory format that
+is never persisted). The runtime uploads every group into one device arena
+with a single host-to-device copy instead of one small tensor per array per
+group (inference.py:393-432), and decodes a block with one launch per dtype
+instead of one per (layout, staging) pair.
+"""
+
+from __future__ import annotations
+
+import functools
+from collections import defaultdict
+from dataclasses import dataclass, field
+from functools import partial
+
+import numpy as np
+import torch
+from torch import nn
+
+from neuralzip_b200 import _native
+from neuralzip_b200.dtypes import DTYPES, DTypeSpec
+from neuralzip_b200.gpu import decoder as gpu_decoder
+from neuralzip_b200.utils import _stream_chunk_size
+
+try:  # transformers is optional for the core path
+    from transformers.pytorch_utils import Conv1D
+except Exception:  # pragma: no cover - exercised only without transformers
+    class Conv1D(nn.Module):  # type: ignore[no-redef]
+        pass
+
+RUNTIME_ATTRIBUTE = "neuralzip_runtime"
+_GPU_WEIGHT_TYPES = (nn.Linear, nn.Conv2d, Conv1D)
+ARENA_ALIGN = 128
+WORKSPACE_ALIGN_BYTES = 128
+
+
+@dataclass(frozen=True)
+class GPUCodebook:
+    """Code lengths/values of one codebook and its tile decode table.
+
+    Validation mirrors neuralzip/gpu/inference.py:28-75: singleton codes are
+    at most 12 bits, pair (mixed) codes at most 56, the alphabet must match
+    the pair vocabulary, and every 12-bit prefix must decode."""
+
+    code_lengths: tuple[int, ...]
+    code_values: tuple[int, ...]
+    vocab: bytes = b""
+    max_bits: int = field(init=False)
+    decode_lut: object = field(init=False, repr=False, compare=False)
+    native: object = field(init=False, repr=False, compare=False)
+
+    def __post_init__(self):
+        longest = max(self.code_lengths, default=0)
+        if longest > (56 if self.vocab else 12):
+            raise ValueError("The GPU codebook exceeds its decoder's code-length limit.")
+        object.__setattr__(self, "max_bits", min(12, longest))
+        if not longest:
+            object.__setattr__(self, "decode_lut", ())
+            object.__setattr__(self, "native", None)
+            return
+        if len(self.code_lengths) != 256 + len(self.vocab) // 2:
+            raise ValueError("The GPU alphabet does not match its pair vocabulary.")
+        if len(self.code_values) != len(self.code_lengths):
+            raise ValueError("Code values must match code lengths.")
+        try:
+            book = _native.NativeCodebook(bytes(self.code_lengths), self.code_values, bytes(self.vocab))
+        except ValueError as error:
+            if "prefix" in str(error) or "cover" in str(error):
+                raise ValueError("The Huffman codebook does not cover every prefix.") from error
+            raise
+        object.__setattr__(self, "native", book)
+        object.__setattr__(self, "decode_lut", book.lut())
+
+    @property
+    def table_words(self):
+        """Words of the decode table the kernel stages (table + suffix tree)."""
+        if self.native is None:
+            return 0
+        return (_native.LUT_ENTRIES + 2 * self.native.tree_nodes + 3) // 4 * 4
+
+
+@dataclass(frozen=True)
+class GPUEncodedSymbols:
+    """Huffman-coded selected lane of one group in the tile layout.
+
+    ``bitstream``: little-endian 32-bit words, bit 31 earliest, zero padded;
+    ``lane_bits``: uint16 bit length per 256-element sub-stream;
+    ``tile_offsets``: bit offset of each 8192-element tile. A raw fragment
+    keeps its bytes in ``bitstream`` with empty sync metadata
+    (neuralzip/gpu/inference.py:319-324)."""
+
+    bitstream: bytes
+    bit_length: int
+    symbol_count: int
+    lane_bits: bytes
+    tile_offsets: tuple[int, ...]
+
+    @property
+    def compressed_bytes(self):
+        return len(self.bitstream) + len(self.lane_bits) + 4 * len(self.tile_offsets)
+
+    # Names of the reference layout's sync metadata.
+    @property
+    def packed_gaps(self):
+        return self.lane_bits
+
+    @property
+    def output_positions(self):
+        return self.tile_offsets
+
+
+@dataclass(frozen=True)
+class GPUEncoded:
+    dtype: DTypeSpec
+    numel: int
+    streams: tuple  # Indexed by byte-lane ID: bytes (raw) or GPUEncodedSymbols.
+
+    @property
+    def raw_bytes(self):
+        return self.numel * self.dtype.element_size
+
+    @property
+    def compressed_bytes(self):
+        return sum(len(s) if isinstance(s, bytes) else s.compressed_bytes for s in self.streams)
+
+    @property
+    def symbols(self):
+        (symbols,) = (s for s in self.streams if isinstance(s, GPUEncodedSymbols))
+        return symbols
+
+
+@functools.lru_cache(maxsize=4096)
+def codebook_from_header(header, vocab=b""):
+    """GPUCodebook of a serialized table (Huff0 header or "NZM1" mixed
+    header), via export_code_table semantics (binding_helpers.h:103-123)."""
+    lengths, values, _longest = _native.export_code_table(header, max_bits=56, vocab=vocab)
+    return GPUCodebook(tuple(lengths), values, bytes(vocab))
+
+
+def _dtype_struct(spec, stream_id):
+    if stream_id != spec.gpu_stream:
+        raise ValueError("GPU stream_id does not match the dtype's coded lane.")
+    return _native.dtype_struct(spec.element_size, spec.bit_reorder, spec.mantissa_bits,
+                                spec.exponent_bits, stream_id)
+
+
+def encode_with_codebook(raw, book, *, dtype, stream_id):
+    """Packs raw element bytes with a GPUCodebook into a GPUEncoded."""
+    dt = _dtype_struct(dtype, stream_id)
+    bits, lens, tile_off, lanes, bit_length = _native.pack_chunk(book.native, raw, dt)
+    numel = len(raw) // dtype.element_size
+    streams = [lane.tobytes() if lane is not None else None for lane in lanes]
+    streams[stream_id] = GPUEncodedSymbols(bits.tobytes(), int(bit_length), numel, lens.tobytes(),
+                                           tuple(int(x) for x in tile_off))
+    return GPUEncoded(dtype, numel, tuple(streams))
+
+
+def encode_gpu_native(raw, codebook_header, *, dtype, stream_id, vocab=b"", codebook_handle=None):
+    """Encodes one chunk's selected lane with a serialized codebook
+    (neuralzip/gpu/inference.py:111-131). ``codebook_handle`` may be a
+    GPUCodebook to skip re-reading the header."""
+    raw = bytes(raw)
+    book = codebook_handle if isinstance(codebook_handle, GPUCodebook) else codebook_from_header(
+        bytes(codebook_header), bytes(vocab))
+    return encode_with_codebook(raw, book, dtype=dtype, stream_id=stream_id)
+
+
+def encode_raw_fragment(raw, *, dtype, stream_id):
+    """Raw fragment: every lane stored as bytes, the selected one wrapped."""
+    lanes = _native.split_lanes(bytes(raw), _dtype_struct(dtype, stream_id))
+    numel = len(raw) // dtype.element_size
+    streams = [lane.tobytes() for lane in lanes]
+    streams[stream_id] = GPUEncodedSymbols(streams[stream_id], 8 * numel, numel, b"", ())
+    return GPUEncoded(dtype, numel, tuple(streams))
+
+
+@dataclass(frozen=True)
+class LinearWeightBinding:
+    module_name: str
+    tensor_name: str
+    shape: tuple[int, ...]
+    numel: int
+    workspace_offset: int
+
+
+@dataclass(frozen=True)
+class GPUWeightGroup:
+    block_name: str
+    codebook_id: int
+    codebook: GPUCodebook
+    encoded: GPUEncoded
+    bindings: tuple[LinearWeightBinding, ...]
+    workspace_offset: int
+
+    @property
+    def layout(self):
+        dtype = self.encoded.dtype
+        return (
+            dtype.element_size, bool(dtype.bit_reorder), dtype.mantissa_bits, dtype.exponent_bits,
+            dtype.gpu_stream, bool(self.codebook.vocab), max(self.codebook.code_lengths, default=0) > 32,
+        )
+
+
+@dataclass(frozen=True)
+class NeuralZipModelExport:
+    groups: tuple[GPUWeightGroup, ...]
+
+    @property
+    def block_order(self):
+        return tuple(dict.fromkeys(group.block_name for group in self.groups))
+
+    @property
+    def bindings(self):
+        return tuple(dict.fromkeys(binding for group in self.groups for binding in group.bindings))
+
+    @property
+    def workspace_sizes(self):
+        sizes = {}
+        for group in self.groups:
+            dtype = group.encoded.dtype.torch_dtype
+            sizes[dtype] = max(sizes.get(dtype, 0), group.workspace_offset + group.encoded.numel)
+        return sizes
+
+
+@dataclass(frozen=True)
+class _Candidate:
+    block_name: str
+    module_name: str
+    tensor_name: str
+    parameter: nn.Parameter = field(repr=False, compare=False)
+
+
+def _join(parent, child):
+    return f"{parent}.{child}" if parent and child else parent or child
+
+
+def _decode_hook_module(model, block_name):
+    parent_name, _, child_name = block_name.rpartition(".")
+    parent = model.get_submodule(parent_name)
+    # MultiheadAttention reads out_proj.weight without calling the Linear.
+    if child_name == "out_proj" and isinstance(parent, nn.MultiheadAttention):
+        return parent
+    return model.get_submodule(block_name)
+
+
+def _gpu_candidates(model):
+    """Blocks are the outermost ModuleList children whose Linears are not all
+    inside nested lists; other weight modules are hooked individually
+    (neuralzip/gpu/inference.py:232-274)."""
+    possible = [
+        (_join(parent_name, child_name), child)
+        for parent_name, parent in model.named_modules(remove_duplicate=False)
+        if isinstance(parent, nn.ModuleList)
+        for child_name, child in parent._modules.items()
+        if child is not None
+    ]
+    names = {name for name, _ in possible}
+    blocks = []
+    for name, module in possible:
+        if any(name.startswith(parent + ".") for parent, _ in blocks):
+            continue
+        nested = tuple(child + "." for child in names if child.startswith(name + "."))
+        if nested and all(
+            (_join(name, child) + ".").startswith(nested)
+            for child, layer in module.named_modules(remove_duplicate=False)
+            if isinstance(layer, nn.Linear)
+        ):
+            continue
+        blocks.append((name, module))
+    candidates = []
+    for module_name, module in model.named_modules(remove_duplicate=False):
+        if not isinstance(module, _GPU_WEIGHT_TYPES):
+            continue
+        parameter = module._parameters.get("weight")
+        if isinstance(parameter, nn.Parameter):
+            block_name = next(
+                (name for name, _ in blocks if module_name == name or module_name.startswith(name + ".")),
+                module_name,
+            )
+            candidates.append(_Candidate(block_name, module_name, _join(module_name, "weight"), parameter))
+    return tuple(dict.fromkeys(c.block_name for c in candidates)), tuple(candidates)
+
+
+def _unique_candidates(model, candidates):
+    occurrences = defaultdict(int)
+    for _name, parameter in model.named_parameters(remove_duplicate=False):
+        occurrences[id(parameter)] += 1
+    return tuple(c for c in candidates if c.parameter.numel() and occurrences[id(c.parameter)] == 1)
+
+
+def _aligned(offset, element_size):
+    step = max(1, WORKSPACE_ALIGN_BYTES // element_size)
+    return (offset + step - 1) // step * step
+
+
+def _assemble_export(block_order, candidates, compressor):
+    """One GPU group per source chunk (neuralzip/gpu/inference.py:288-336).
+    Tensor offsets inside a block workspace are rounded up to 128 bytes so
+    every group's output is 16-byte aligned for the vector stores."""
+    payloads = {int(p.codebook_id): p for p in compressor.export_codebooks()}
+    codebooks = {}
+    block_index = {name: index for index, name in enumerate(block_order)}
+    workspace_offsets = defaultdict(int)
+    groups = []
+    for member in sorted(candidates, key=lambda c: (block_index[c.block_name], c.module_name)):
+        parameter = member.parameter
+        spec = DTYPES[parameter.dtype]
+        stream_id = spec.gpu_stream
+        key = compressor._transfer_plan_key(member.tensor_name, parameter, stream_id)
+        modes = compressor._transfer_chunk_modes[key]
+        step = _stream_chunk_size(compressor.chunk_size, spec.element_size)
+        raw = parameter.detach().cpu().contiguous().reshape(-1).view(torch.uint8).numpy().tobytes()
+        ws_key = (member.block_name, parameter.dtype)
+        workspace_offset = _aligned(workspace_offsets[ws_key], spec.element_size)
+        binding = LinearWeightBinding(member.module_name, member.tensor_name, tuple(parameter.shape),
+                                      parameter.numel(), workspace_offset)
+        fragments = []
+        for chunk, mode in enumerate(modes):
+            start = chunk * step
+            part = raw[start * spec.element_size:(start + step) * spec.element_size]
+            codebook_id = mode.get("codebook_id", -1) if mode.get("kind", "raw") != "raw" else -1
+            if codebook_id not in codebooks:
+                if codebook_id == -1:
+                    codebooks[-1] = GPUCodebook((), ())
+                else:
+                    payload = payloads[codebook_id]
+                    codebooks[codebook_id] = codebook_from_header(bytes(payload.codebook), bytes(payload.vocab))
+            if codebook_id == -1:
+                encoded = encode_raw_fragment(part, dtype=spec, stream_id=stream_id)
+            else:
+                encoded = encode_with_codebook(part, codebooks[codebook_id], dtype=spec, stream_id=stream_id)
+            fragments.append(GPUWeightGroup(member.block_name, codebook_id, codebooks[codebook_id], encoded,
+                                            (binding,), workspace_offset + start))
+        if sum(group.encoded.compressed_bytes for group in fragments) >= len(raw):
+            continue
+        groups.extend(fragments)
+        workspace_offsets[ws_key] = workspace_offset + parameter.numel()
+    return NeuralZipModelExport(tuple(groups))
+
+
+def export_model_for_gpu(model, setup, *, allowed_dtypes=DTYPES):
+    """Exports the frozen chunk tables, including adaptive singleton/pair
+    codes (neuralzip/gpu/inference.py:339-358)."""
+    from neuralzip_b200.compressor import NeuralZipCompressor
+
+    blocks, candidates = _gpu_candidates(model)
+    candidates = _unique_candidates(model, candidates)
+    candidates = tuple(
+        c for c in candidates
+        if c.parameter.dtype in DTYPES and c.parameter.dtype in allowed_dtypes and c.parameter.is_contiguous()
+    )
+    if not candidates:
+        return NeuralZipModelExport(())
+    compressor = NeuralZipCompressor(setup, gpu=True)
+    compressor.prepare_gpu_transfer_target(tuple((c.tensor_name, c.parameter) for c in candidates))
+    return _assemble_export(blocks, candidates, compressor)
+
+
+def _binding_module(model, binding):
+    module = model.get_submodule(binding.module_name)
+    if not isinstance(module, _GPU_WEIGHT_TYPES):
+        raise TypeError(f"{binding.module_name!r} is not a supported weight module.")
+    return module
+
+
+def _binding_view(workspaces, dtype, binding):
+    offset = binding.workspace_offset
+    return workspaces[dtype][offset:offset + binding.numel].view(binding.shape)
+
+
+def _group_arrays(group):
+    """Host arrays of one group in upload order: name -> uint8 view."""
+    encoded = group.encoded
+    symbols = encoded.symbols
+    stream = encoded.dtype.gpu_stream
+    arrays = {}
+    if group.codebook.max_bits:
+        arrays["bits"] = symbols.bitstream
+        arrays["lens"] = symbols.lane_bits
+        arrays["tile_off"] = np.asarray(symbols.tile_offsets, dtype=np.uint32).tobytes()
+    for lane, data in enumerate(encoded.streams):
+        if lane == stream:
+            if not group.codebook.max_bits:
+                arrays[f"lane{lane}"] = symbols.bitstream
+        else:
+            arrays[f"lane{lane}"] = data
+    return arrays
+
+
+@dataclass(frozen=True)
+class _UploadedGroup:
+    group: GPUWeightGroup
+    device: object  # decoder.DeviceGroup
+
+    @property
+    def layout(self):
+        return self.group.layout
+
+
+class NeuralZipRuntime:
+    """Runtime attached to one model on one CUDA device."""
+
+    def __init__(self, model, exported, device):
+        self.model = model
+        self.export = exported
+        self.device = torch.device(device)
+        self._decoder = gpu_decoder.default_decoder()
+        self._hook_handles = []
+        self.workspaces = {
+            dtype: torch.empty(size, dtype=dtype, device=self.device)
+            for dtype, size in exported.workspace_sizes.items()
+        }
+        # Decode tables: one row of LUT_WORDS words per codebook id.
+        book_ids = sorted({g.codebook_id for g in exported.groups if g.codebook.max_bits})
+        self._lut_rows = {cid: row for row, cid in enumerate(book_ids)}
+        books = {g.codebook_id: g.codebook for g in exported.groups}
+        if book_ids:
+            table = np.stack([np.asarray(books[cid].decode_lut, dtype=np.uint32) for cid in book_ids])
+            self.decode_tables = torch.from_numpy(table).to(self.device)
+        else:
+            self.decode_tables = torch.zeros((1, _native.LUT_WORDS), dtype=torch.int32, device=self.device)
+        # One arena for every group's arrays.
+        offsets = []
+        cursor = 0
+        for group in exported.groups:
+            placed = {}
+            for name, data in _group_arrays(group).items():
+                cursor = (cursor + ARENA_ALIGN - 1) // ARENA_ALIGN * ARENA_ALIGN
+                placed[name] = (cursor, data)
+                cursor += len(data)
+            offsets.append(placed)
+        host = np.zeros(max(cursor, 1), dtype=np.uint8)
+        for placed in offsets:
+            for start, data in placed.values():
+                host[start:start + len(data)] = np.frombuffer(data, dtype=np.uint8)
+        self.arena = torch.from_numpy(host).to(self.device)
+        base = self.arena.data_ptr()
+        lut_base = self.decode_tables.data_ptr()
+        row_bytes = _native.LUT_WORDS * 4
+        uploaded = []
+        for group, placed in zip(exported.groups, offsets):
+            spec = group.encoded.dtype
+
+            def addr(name, placed=placed):
+                return base + placed[name][0] if name in placed else 0
+
+            output = self.workspaces[spec.torch_dtype][group.workspace_offset:
+                                                       group.workspace_offset + group.encoded.numel]
+            coded = bool(group.codebook.max_bits)
+            row = self._lut_rows.get(group.codebook_id) if coded else None
+            device_group = gpu_decoder.DeviceGroup(
+                spec=spec, numel=group.encoded.numel,
+                lut_index=row if coded else _native.RAW_LUT,
+                lut_ptr=lut_base + row * row_bytes if coded else 0,
+                lut_words=group.codebook.table_words,
+                bits=addr("bits"), lens=addr("lens"), tile_off=addr("tile_off"),
+                lanes=tuple(addr(f"lane{lane}") for lane in range(4)),
+                out=output.data_ptr(), output=output,
+            )
+            uploaded.append(_UploadedGroup(group, device_group))
+        by_block = defaultdict(list)
+        for item in uploaded:
+            by_block[item.group.block_name].append(item)
+        self._groups_by_block = {name: tuple(by_block[name]) for name in exported.block_order}
+        self._prepared_batches = {}
+        for name, items in self._groups_by_block.items():
+            per_dtype = defaultdict(list)
+            for item in items:
+                per_dtype[item.group.encoded.dtype.name].append(item.device)
+            self._prepared_batches[name] = tuple(
+                self._decoder.prepare_batch(batch) for batch in per_dtype.values()
+            )
+        torch.cuda.synchronize(self.device)
+
+    @classmethod
+    def attach(cls, model, exported, *, device=None):
+        if hasattr(model, RUNTIME_ATTRIBUTE):
+            raise RuntimeError("This model already has a NeuralZip runtime.")
+        if not exported.groups:
+            raise ValueError("The setup produced no GPU-compressible weights.")
+        if device is None:
+            current = next(model.parameters()).device
+            device = current if current.type == "cuda" else "cuda"
+        device = torch.device(device)
+        if device.type != "cuda":
+            raise ValueError("NeuralZip GPU inference requires a CUDA device.")
+        if device.index is None:
+            device = torch.device("cuda", torch.cuda.current_device())
+        decoder = gpu_decoder.default_decoder()
+        for group in exported.groups:
+            decoder.prepare_group(device.index, group)
+        for binding in exported.bindings:
+            module = _binding_module(model, binding)
+            module._parameters.pop("weight", None)
+            module.__dict__.pop("weight", None)
+        model.to(device).eval()
+        runtime = cls(model, exported, device)
+        runtime._install()
+        return runtime
+
+    def _install(self):
+        for items in self._groups_by_block.values():
+            for item in items:
+                for binding in item.group.bindings:
+                    _binding_module(self.model, binding).__dict__["weight"] = _binding_view(
+                        self.workspaces, item.group.encoded.dtype.torch_dtype, binding)
+        for block_name in self.export.block_order:
+            handle = _decode_hook_module(self.model, block_name).register_forward_pre_hook(
+                partial(self._decode_block, block_name), prepend=True)
+            self._hook_handles.append(handle)
+        setattr(self.model, RUNTIME_ATTRIBUTE, self)
+
+    def _decode_block(self, block_name, _module=None, _args=None):
+        for prepared in self._prepared_batches[block_name]:
+            self._decoder.decode_batch(prepared)
+
+    def check_status(self):
+        """Raises if any decode launch reported a corrupt table."""
+        for batches in self._prepared_batches.values():
+            for prepared in batches:
+                self._decoder.check_status(prepared)
+
+    @torch.no_grad()
+    def materialized_weights(self):
+        """Yield compressed weights as bit-exact CPU tensors, one block at a time."""
+        yielded = set()
+        for block_name in self.export.block_order:
+            self._decode_block(block_name)
+            torch.cuda.synchronize(self.device)
+            for item in self._groups_by_block[block_name]:
+                for binding in item.group.bindings:
+                    if binding.tensor_name in yielded:
+                        continue
+                    yielded.add(binding.tensor_name)
+                    weight = _binding_view(self.workspaces, item.group.encoded.dtype.torch_dtype, binding)
+                    yield binding.tensor_name, weight.detach().to("cpu", copy=True)

@@ -1,0 +1,230 @@
+"""GPU parity of the tile decode kernel against the oracle (bit-exact).
+
+Every expected tensor is computed on the CPU by the oracle: the reference
+GPU layout is encoded and decoded with the reference's kernel semantics
+(oracle/nz_oracle.c: oz_ref_encode / oz_ref_decode) and the lanes merged
+(oz_restore). The oracle output is also checked against the original bits,
+which is the reference's own criterion for every decode.
+"""
+
+import numpy as np
+import pytest
+import torch
+from torch import nn
+
+import helpers as H
+from neuralzip_b200 import _native
+from neuralzip_b200.dtypes import DTYPES
+from neuralzip_b200.gpu import decoder as gpu_decoder
+from neuralzip_b200.gpu.inference import (
+    GPUCodebook,
+    GPUWeightGroup,
+    LinearWeightBinding,
+    NeuralZipModelExport,
+    NeuralZipRuntime,
+    encode_raw_fragment,
+    encode_with_codebook,
+)
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def exact(a, b):
+    return torch.equal(a.cpu().contiguous().view(torch.uint8), b.cpu().contiguous().view(torch.uint8))
+
+
+def oracle_expected(raw, spec, lengths, values, vocab):
+    """Oracle decode of the reference GPU layout, merged with the raw lanes."""
+    lanes = O.split(raw, spec)
+    sel = lanes[spec.gpu_stream]
+    layout = O.ref_encode(sel, lengths, values, vocab)
+    lut, max_bits = O.ref_lut(lengths, values, vocab)
+    decoded = O.ref_decode(layout, lut, max_bits, bool(vocab), len(sel))
+    lanes[spec.gpu_stream] = decoded
+    out = O.restore(lanes, spec)
+    assert out.tobytes() == bytes(raw), "oracle does not reproduce the original bits"
+    return out
+
+
+def single_group_model(raw, spec, book):
+    original = torch.frombuffer(bytearray(raw), dtype=spec.torch_dtype).reshape(1, -1)
+    model = nn.Module()
+    model.layers = nn.ModuleList([nn.Linear(original.numel(), 1, bias=False, dtype=spec.torch_dtype)])
+    with torch.no_grad():
+        model.layers[0].weight.copy_(original)
+    encoded = encode_with_codebook(raw, book, dtype=spec, stream_id=spec.gpu_stream)
+    binding = LinearWeightBinding("layers.0", "layers.0.weight", tuple(original.shape), original.numel(), 0)
+    export = NeuralZipModelExport((GPUWeightGroup("layers.0", 0, book, encoded, (binding,), 0),))
+    return model, export, original
+
+
+@pytest.mark.parametrize("max_bits", [12, 32, 33, 56])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+def test_segment_boundaries(max_bits, dtype):
+    spec = DTYPES[dtype]
+    lengths = H.segment_lengths(max_bits)
+    values = O.mixed_codes(lengths)
+    book = GPUCodebook(tuple(lengths), tuple(int(v) for v in values), H.VOCAB)
+    raw = H.lanes_with(H.segment_symbols(), spec)
+    expected = oracle_expected(raw, spec, lengths, values, H.VOCAB)
+    model, export, original = single_group_model(raw, spec, book)
+    runtime = NeuralZipRuntime.attach(model, export, device="cuda:0")
+    for _ in range(2):
+        for workspace in runtime.workspaces.values():
+            workspace.view(torch.uint8).fill_(0xA5)
+        got = dict(runtime.materialized_weights())["layers.0.weight"]
+        assert exact(got, original)
+        assert got.view(torch.uint8).numpy().tobytes() == expected.tobytes()
+    runtime.check_status()
+
+
+def test_long_codes_bf16():
+    spec = DTYPES[torch.bfloat16]
+    lengths = H.long_code_lengths()
+    assert max(lengths) > 12
+    values = O.mixed_codes(lengths)
+    book = GPUCodebook(tuple(lengths), tuple(int(v) for v in values), H.VOCAB)
+    assert book.native.tree_nodes > 0
+    symbols = np.array([127] * 70000 + list(range(256)) * 3 + [126], dtype=np.uint8)
+    raw = H.lanes_with(symbols, spec)
+    expected = oracle_expected(raw, spec, lengths, values, H.VOCAB)
+    model, export, original = single_group_model(raw, spec, book)
+    runtime = NeuralZipRuntime.attach(model, export, device="cuda:0")
+    got = dict(runtime.materialized_weights())["layers.0.weight"]
+    assert exact(got, original)
+    assert got.view(torch.uint8).numpy().tobytes() == expected.tobytes()
+
+
+def _gaussian_export(spec, numel, sigmas, chunk, seed=0, raw_chunk=None, mixed=True):
+    """One tensor cut into `chunk`-element groups with per-chunk sigma;
+    singleton and mixed codebooks alternate, one chunk may stay raw."""
+    pieces = [H.gaussian_raw(min(chunk, numel - s), sigmas[i % len(sigmas)], spec.torch_dtype, seed + i)
+              for i, s in enumerate(range(0, numel, chunk))]
+    raw = b"".join(pieces)
+    original = torch.frombuffer(bytearray(raw), dtype=spec.torch_dtype).reshape(1, -1)
+    binding = LinearWeightBinding("layers.0", "layers.0.weight", tuple(original.shape), numel, 0)
+    groups, books = [], {}
+    for i, piece in enumerate(pieces):
+        sel = H.selected_lane(piece, spec)
+        start = i * chunk
+        if raw_chunk is not None and i == raw_chunk:
+            enc = encode_raw_fragment(piece, dtype=spec, stream_id=spec.gpu_stream)
+            groups.append(GPUWeightGroup("layers.0", -1, GPUCodebook((), ()), enc, (binding,), start))
+            continue
+        if mixed and spec.exponent_stream is not None and i % 2 == 1:
+            lengths, vocab = H.mixed_book_for(sel)
+            book = GPUCodebook(tuple(lengths), tuple(int(v) for v in O.mixed_codes(lengths)), vocab)
+        else:
+            header, _ = _native.huff0_build(np.bincount(sel, minlength=256) + 1, 12)
+            lengths, values, _, _ = _native.huff0_read(header)
+            book = GPUCodebook(tuple(lengths), values)
+        books[i] = book
+        enc = encode_with_codebook(piece, book, dtype=spec, stream_id=spec.gpu_stream)
+        groups.append(GPUWeightGroup("layers.0", i, book, enc, (binding,), start))
+    return raw, original, NeuralZipModelExport(tuple(groups))
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+def test_multi_codebook_batch_with_raw_fragment(dtype):
+    spec = DTYPES[dtype]
+    numel = 5 * 131072 + 4099  # odd tail chunk
+    raw, original, export = _gaussian_export(spec, numel, [0.02, 0.002, 0.2, 1.0], 131072, raw_chunk=2)
+    model = nn.Module()
+    model.layers = nn.ModuleList([nn.Linear(numel, 1, bias=False, dtype=dtype)])
+    runtime = NeuralZipRuntime.attach(model, export, device="cuda:0")
+    for workspace in runtime.workspaces.values():
+        workspace.view(torch.uint8).fill_(0xA5)
+    got = dict(runtime.materialized_weights())["layers.0.weight"]
+    assert exact(got, original)
+    runtime.check_status()
+
+
+def _device_group(raw, spec, book, out_tensor, arena):
+    """Uploads one group by hand; returns its DeviceGroup."""
+    enc = encode_with_codebook(raw, book, dtype=spec, stream_id=spec.gpu_stream)
+    sym = enc.symbols
+    pieces = {"bits": sym.bitstream, "lens": sym.lane_bits,
+              "tile_off": np.asarray(sym.tile_offsets, dtype=np.uint32).tobytes()}
+    for lane, data in enumerate(enc.streams):
+        if lane != spec.gpu_stream:
+            pieces[f"lane{lane}"] = data
+    addr = {}
+    for name, data in pieces.items():
+        t = torch.frombuffer(bytearray(data), dtype=torch.uint8).to("cuda")
+        arena.append(t)
+        addr[name] = t.data_ptr()
+    lut = torch.from_numpy(np.asarray(book.decode_lut, dtype=np.uint32).view(np.int32)).to("cuda")
+    arena.append(lut)
+    return gpu_decoder.DeviceGroup(
+        spec=spec, numel=enc.numel, lut_index=id(book) & 0xFFFF, lut_ptr=lut.data_ptr(),
+        lut_words=book.table_words, bits=addr["bits"], lens=addr["lens"], tile_off=addr["tile_off"],
+        lanes=tuple(addr.get(f"lane{lane}", 0) for lane in range(4)), out=out_tensor.data_ptr(),
+        output=out_tensor)
+
+
+@pytest.mark.parametrize("offset_elems", [0, 1, 3])
+def test_guard_bytes_and_unaligned_outputs(offset_elems):
+    """Writes stay inside [out, out + numel); unaligned outputs take the
+    scalar path and still match."""
+    spec = DTYPES[torch.bfloat16]
+    numel = 3 * 8192 + 777
+    raw = H.gaussian_raw(numel, 0.02, torch.bfloat16, 7)
+    sel = H.selected_lane(raw, spec)
+    lengths, vocab = H.mixed_book_for(sel)
+    book = GPUCodebook(tuple(lengths), tuple(int(v) for v in O.mixed_codes(lengths)), vocab)
+    guard = 4096
+    buffer = torch.full((numel + 2 * guard,), -1, dtype=torch.int16, device="cuda")
+    out = buffer[guard + offset_elems:guard + offset_elems + numel].view(torch.bfloat16)
+    arena = []
+    dg = _device_group(raw, spec, book, out, arena)
+    decoder = gpu_decoder.default_decoder()
+    prepared = decoder.prepare_batch([dg])
+    decoder.decode_batch(prepared)
+    torch.cuda.synchronize()
+    host = buffer.cpu()
+    assert bytes(out.cpu().view(torch.uint8).numpy()) == raw
+    assert (host[:guard + offset_elems] == -1).all()
+    assert (host[guard + offset_elems + numel:] == -1).all()
+    decoder.check_status(prepared)
+
+
+def test_c_abi_launch_by_hand():
+    """Builds nz_group / nz_work / nz_cta records directly and calls
+    nz_decode_launch, without the Python decoder."""
+    spec = DTYPES[torch.float32]
+    numel = 2 * 8192 + 5
+    raw = H.gaussian_raw(numel, 0.02, torch.float32, 3)
+    sel = H.selected_lane(raw, spec)
+    lengths, vocab = H.mixed_book_for(sel)
+    book = GPUCodebook(tuple(lengths), tuple(int(v) for v in O.mixed_codes(lengths)), vocab)
+    out = torch.empty(numel, dtype=torch.float32, device="cuda")
+    arena = []
+    dg = _device_group(raw, spec, book, out, arena)
+    groups = np.zeros(1, dtype=_native.GROUP_DTYPE)
+    groups[0] = (dg.bits, dg.lens, dg.tile_off, dg.lanes, dg.out, numel, 0)
+    works = np.array([(0, t) for t in range(dg.tiles)], dtype=_native.WORK_DTYPE)
+    ctas = np.array([(0, 0, dg.tiles, dg.lut_words)], dtype=_native.CTA_DTYPE)
+    luts = np.array([dg.lut_ptr], dtype=np.uint64)
+    dev = [torch.from_numpy(a.view(np.uint8).copy()).cuda() for a in (groups, works, ctas, luts)]
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    launch = _native.Launch()
+    launch.dtype = _native.dtype_struct(4, 1, 23, 8, 3)
+    launch.warps_per_cta = 4
+    launch.groups, launch.works, launch.ctas, launch.luts = (t.data_ptr() for t in dev)
+    launch.status = status.data_ptr()
+    launch.n_ctas = 1
+    _native.decode_launch(launch, torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert bytes(out.cpu().view(torch.uint8).numpy()) == raw
+    assert int(status.item()) == 0
+
+
+def test_launch_rejects_bad_geometry():
+    launch = _native.Launch()
+    launch.dtype = _native.dtype_struct(2, 1, 7, 8, 1)
+    launch.warps_per_cta = 5
+    launch.n_ctas = 1
+    launch.groups = launch.works = launch.ctas = launch.luts = 1
+    with pytest.raises(ValueError):
+        _native.decode_launch(launch, 0)

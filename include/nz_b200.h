@@ -158,6 +158,33 @@ int nz_pack_many(nz_pack_job* jobs, uint64_t count, const nz_dtype* dt,
 int nz_split_lanes(const uint8_t* raw, uint64_t numel, const nz_dtype* dt,
                    uint8_t* const* lanes);
 
+/* ---- host: CPU storage codec (storage format v2 payloads) ----------- */
+
+/* Greedy pair parse counts (neuralzip/native/mixed_huffman.h:85-115):
+ * counts[token] += occurrences; counts has 256 + vocab_size / 2 entries. */
+int nz_count_tokens(const uint8_t* data, uint64_t size, const uint8_t* vocab,
+                    uint32_t vocab_size, uint64_t* counts);
+/* Exponent-field histograms (256 bins) of consecutive `step`-element chunks
+ * of raw elements, added into histograms[chunk * 256 + exponent]; the
+ * per-chunk distributions setup clusters (neuralzip/setup.py:91-141). */
+int nz_exponent_histograms(const uint8_t* raw, uint64_t numel, const nz_dtype* dt,
+                           uint64_t step, uint64_t* histograms);
+/* Mixed frame (mixed_huffman.h:127-178). *written = 0 when the frame does
+ * not fit `cap`; out may be NULL to measure only. */
+int nz_mixed_encode(const nz_codebook* codebook, const uint8_t* data,
+                    uint64_t size, uint8_t* out, uint64_t cap, uint64_t* written);
+/* Inverse of nz_mixed_encode with the validation of mixed_huffman.h:180-240. */
+int nz_mixed_decode(const nz_codebook* codebook, const uint8_t* frame,
+                    uint64_t size, uint8_t* out, uint64_t expected);
+/* Huff0 4-stream block of a singleton codebook (RFC 8878 section 4.2.2;
+ * replaces HUF_compress4X_usingCTable, codebooks.h:131-141). *written = 0
+ * when it does not fit; out may be NULL to measure only. */
+int nz_huff0_encode(const nz_codebook* codebook, const uint8_t* data,
+                    uint64_t size, uint8_t* out, uint64_t cap, uint64_t* written);
+/* Replaces HUF_decompress4X_usingDTable (codebooks.h:156-206). */
+int nz_huff0_decode(const nz_codebook* codebook, const uint8_t* block,
+                    uint64_t size, uint8_t* out, uint64_t count);
+
 /* ---- device: decode --------------------------------------------------- */
 
 /* One group of a decode launch (device-resident array). Pointers are

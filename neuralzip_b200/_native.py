@@ -69,7 +69,8 @@ assert GROUP_DTYPE.itemsize == 72 and WORK_DTYPE.itemsize == 8 and CTA_DTYPE.ite
 EXPORTS = (
     "nz_export_code_table", "nz_codebook_create", "nz_codebook_destroy", "nz_codebook_info",
     "nz_codebook_lut", "nz_huff0_build", "nz_huff0_read", "nz_pack_bound", "nz_pack_chunk",
-    "nz_pack_many", "nz_split_lanes", "nz_decode_launch", "nz_decode_smem_bytes", "nz_last_error",
+    "nz_pack_many", "nz_split_lanes", "nz_exponent_histograms", "nz_count_tokens", "nz_mixed_encode", "nz_mixed_decode",
+    "nz_huff0_encode", "nz_huff0_decode", "nz_decode_launch", "nz_decode_smem_bytes", "nz_last_error",
     "nz_abi_version",
 )
 
@@ -116,6 +117,12 @@ def _declare(lib):
                           c.c_void_p, c.c_uint64, c.c_void_p, c.c_uint64, c.c_void_p, u64p, u64p],
         "nz_pack_many": [c.POINTER(PackJob), c.c_uint64, c.POINTER(Dtype), c.c_int32],
         "nz_split_lanes": [c.c_void_p, c.c_uint64, c.POINTER(Dtype), c.c_void_p],
+        "nz_count_tokens": [c.c_void_p, c.c_uint64, c.c_void_p, c.c_uint32, c.c_void_p],
+        "nz_exponent_histograms": [c.c_void_p, c.c_uint64, c.POINTER(Dtype), c.c_uint64, c.c_void_p],
+        "nz_mixed_encode": [c.c_void_p, c.c_void_p, c.c_uint64, c.c_void_p, c.c_uint64, u64p],
+        "nz_mixed_decode": [c.c_void_p, c.c_void_p, c.c_uint64, c.c_void_p, c.c_uint64],
+        "nz_huff0_encode": [c.c_void_p, c.c_void_p, c.c_uint64, c.c_void_p, c.c_uint64, u64p],
+        "nz_huff0_decode": [c.c_void_p, c.c_void_p, c.c_uint64, c.c_void_p, c.c_uint64],
         "nz_decode_launch": [c.POINTER(Launch), c.c_void_p],
         "nz_decode_smem_bytes": [c.c_uint32, u32p],
         "nz_last_error": [c.c_char_p, c.c_size_t],
@@ -272,6 +279,74 @@ def pack_many(jobs, dt, threads=0):
     array = (PackJob * len(jobs))(*jobs)
     check(lib.nz_pack_many(array, len(jobs), ctypes.byref(dt), int(threads)))
     return array
+
+
+# ---- CPU storage codec ------------------------------------------------------------
+
+def _bytes_array(data):
+    if isinstance(data, np.ndarray):
+        return np.ascontiguousarray(data.reshape(-1).view(np.uint8))
+    return np.frombuffer(memoryview(data).cast("B"), dtype=np.uint8)
+
+
+def count_tokens(data, vocab=b"", counts=None):
+    """Adds greedy pair-parse token counts of `data` into `counts`."""
+    lib = load()
+    data = _bytes_array(data)
+    vocab = bytes(vocab)
+    if counts is None:
+        counts = np.zeros(256 + len(vocab) // 2, dtype=np.uint64)
+    vocab_array = np.frombuffer(vocab, dtype=np.uint8) if vocab else None
+    check(lib.nz_count_tokens(_ptr(data) if len(data) else None, len(data), _ptr(vocab_array), len(vocab),
+                              _ptr(counts)))
+    return counts
+
+
+def exponent_histograms(raw, dt, step):
+    """(chunks, 256) exponent histograms of consecutive `step`-element chunks."""
+    lib = load()
+    raw = _bytes_array(raw)
+    numel = len(raw) // dt.elem_size
+    chunks = (numel + step - 1) // step
+    out = np.zeros((chunks, 256), dtype=np.uint64)
+    check(lib.nz_exponent_histograms(_ptr(raw) if numel else None, numel, ctypes.byref(dt), int(step), _ptr(out)))
+    return out
+
+
+def _encode(fn, codebook, data, cap, measure):
+    lib = load()
+    data = _bytes_array(data)
+    written = ctypes.c_uint64()
+    out = None if measure else np.empty(max(int(cap), 1), dtype=np.uint8)
+    check(getattr(lib, fn)(codebook.handle, _ptr(data) if len(data) else None, len(data), _ptr(out), int(cap),
+                           ctypes.byref(written)))
+    return written.value if measure else out[:written.value].tobytes()
+
+
+def mixed_encode(codebook, data, cap, measure=False):
+    """Mixed frame bytes (b"" when it does not fit cap), or its size when measuring."""
+    return _encode("nz_mixed_encode", codebook, data, cap, measure)
+
+
+def huff0_encode(codebook, data, cap, measure=False):
+    """Huff0 4-stream block bytes (b"" when it does not fit cap), or its size."""
+    return _encode("nz_huff0_encode", codebook, data, cap, measure)
+
+
+def mixed_decode(codebook, frame, expected, out=None):
+    lib = load()
+    frame = _bytes_array(frame)
+    out = np.empty(expected, dtype=np.uint8) if out is None else out
+    check(lib.nz_mixed_decode(codebook.handle, _ptr(frame), len(frame), _ptr(out), int(expected)))
+    return out
+
+
+def huff0_decode(codebook, block, count, out=None):
+    lib = load()
+    block = _bytes_array(block)
+    out = np.empty(count, dtype=np.uint8) if out is None else out
+    check(lib.nz_huff0_decode(codebook.handle, _ptr(block), len(block), _ptr(out), int(count)))
+    return out
 
 
 # ---- decode -----------------------------------------------------------------------

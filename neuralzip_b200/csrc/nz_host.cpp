@@ -181,6 +181,24 @@ void Codebook::build_lut() {
         return 2;
     };
 
+    single.assign(NZ_LUT_ENTRIES, 0);
+    for (uint32_t prefix = 0; prefix < NZ_LUT_ENTRIES; ++prefix) {
+        int node = 0;
+        uint32_t depth = 0;
+        while (trie[node].symbol < 0 && depth < NZ_LUT_BITS) {
+            node = trie[node].child[(prefix >> (NZ_LUT_BITS - 1 - depth)) & 1U];
+            ++depth;
+            if (node < 0) throw Error(NZ_EVALUE, "The Huffman codebook does not cover every prefix.");
+        }
+        if (trie[node].symbol >= 0) {
+            uint32_t value = 0;
+            const uint32_t count = token_bytes(trie[node].symbol, &value);
+            single[prefix] = value | (count << 16) | (depth << 20);
+        } else {
+            single[prefix] = static_cast<uint32_t>(trie[node].suffix);
+        }
+    }
+
     lut.assign(NZ_LUT_WORDS, 0);
     for (uint32_t prefix = 0; prefix < NZ_LUT_ENTRIES; ++prefix) {
         uint32_t pos = 0, nbytes = 0, bytes = 0;

@@ -28,7 +28,11 @@ struct Codebook {
     std::vector<uint64_t> codes;
     std::vector<uint16_t> vocab;        // pair k -> first | second << 8
     std::vector<uint16_t> pair_tokens;  // (first | second << 8) -> 256 + k, 0 = none
-    std::vector<uint32_t> lut;          // NZ_LUT_WORDS words
+    std::vector<uint32_t> lut;          // NZ_LUT_WORDS words (tile kernel table)
+    // Host single-token table for the CPU codecs: for a 12-bit window,
+    // bytes (bits 0..15) | byte count << 16 | code length << 20, or a
+    // suffix-tree node index with a zero byte count for longer codes.
+    std::vector<uint32_t> single;
 
     void build(const uint8_t* lengths, const uint64_t* values, uint32_t nsym,
                const uint8_t* vocab, uint32_t vocab_size);
@@ -44,6 +48,11 @@ void pack_chunk(const Codebook& cb, const uint8_t* raw, uint64_t numel, const nz
                 uint32_t* bits, uint64_t bits_cap, uint16_t* lens, uint64_t lens_cap,
                 uint32_t* tile_off, uint64_t tiles_cap, uint8_t* const* lanes,
                 uint64_t* bit_length, uint64_t* words_used);
+uint64_t mixed_encode(const Codebook& cb, const uint8_t* data, uint64_t size, uint8_t* out, uint64_t cap);
+void mixed_decode(const Codebook& cb, const uint8_t* data, uint64_t size, uint8_t* out, uint64_t expected);
+uint64_t huff0_encode(const Codebook& cb, const uint8_t* data, uint64_t size, uint8_t* out, uint64_t cap);
+void huff0_decode(const Codebook& cb, const uint8_t* data, uint64_t size, uint8_t* out, uint64_t count);
+
 void run_jobs(uint64_t count, int threads, const std::function<void(uint64_t)>& job);
 
 // Huff0 table headers (RFC 8878 section 4.2.1): weights -> code lengths and

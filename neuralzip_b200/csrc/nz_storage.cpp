@@ -1,0 +1,365 @@
+// CPU storage codec pieces: token counting, mixed frames and Huff0 4-stream
+// blocks. Setup uses the encoders to size both codebook options
+// (neuralzip/setup.py:207-249); the storage format v2 save/load path uses
+// encoders and decoders.
+//
+// Reference behaviour restated here (paths inside the reference project):
+//   count_mixed_tokens      neuralzip/native/mixed_huffman.h:85-115
+//   encode_mixed_block_into mixed_huffman.h:127-178: a 32-byte header of four
+//                           (u32 tokens, u32 bits) pairs, then four MSB-first,
+//                           byte-padded lanes split at source positions
+//                           size * (lane + 1) / 4 without resetting the greedy
+//                           parse; 0 when the frame does not fit `cap`.
+//   decode_mixed_block_into mixed_huffman.h:180-240 (validation included).
+//   encode/decode_huff0     zstd HUF_compress4X_usingCTable /
+//                           HUF_decompress4X_usingDTable (codebooks.h:131-206),
+//                           restated from RFC 8878 section 4.2.2: a 6-byte jump
+//                           table of three little-endian u16 stream sizes, four
+//                           segments of (size + 3) / 4 symbols (the last takes
+//                           the rest), each a backward bitstream ending in a
+//                           1-bit marker whose first-read bits are the first
+//                           symbol's code. Byte parity with zstd's output is not
+//                           pinned here (zstd is not vendored by the reference).
+
+#include "nz_b200.h"
+#include "nz_internal.h"
+
+#include <algorithm>
+#include <cstring>
+#include <string>
+#include <vector>
+
+namespace nz {
+namespace {
+
+// LSB-first bit sink used for backward (Huff0) streams.
+struct BackwardWriter {
+    uint8_t* out;
+    uint64_t cap;
+    uint64_t bytes = 0;
+    uint64_t acc = 0;
+    uint32_t n = 0;
+    bool overflow = false;
+    void add(uint64_t value, uint32_t bits) {  // bits <= 32
+        acc |= value << n;
+        n += bits;
+        while (n >= 8) {
+            if (out) {
+                if (bytes >= cap) overflow = true;
+                else out[bytes] = static_cast<uint8_t>(acc);
+            }
+            ++bytes;
+            acc >>= 8;
+            n -= 8;
+        }
+    }
+    void close() {
+        add(1, 1);
+        if (n) {
+            if (out) {
+                if (bytes >= cap) overflow = true;
+                else out[bytes] = static_cast<uint8_t>(acc);
+            }
+            ++bytes;
+            acc = 0;
+            n = 0;
+        }
+    }
+};
+
+}  // namespace
+
+uint64_t mixed_encode(const Codebook& cb, const uint8_t* data, uint64_t size, uint8_t* out, uint64_t cap) {
+    if (cap <= 32) return 0;
+    const bool pairs = !cb.pair_tokens.empty();
+    uint64_t cursor = 32, source = 0;
+    for (unsigned lane = 0; lane < 4; ++lane) {
+        const uint64_t end = size * (lane + 1) / 4;
+        uint64_t tokens = 0, bits = 0, acc = 0;
+        uint32_t pending = 0;
+        auto put_byte = [&](uint8_t b) -> bool {
+            if (cursor >= cap) return false;
+            if (out) out[cursor] = b;
+            ++cursor;
+            return true;
+        };
+        while (source < end) {
+            uint32_t token = data[source];
+            if (pairs && source + 1 < size) {
+                const uint16_t pair = cb.pair_tokens[token | (static_cast<uint32_t>(data[source + 1]) << 8)];
+                if (pair) token = pair;
+            }
+            source += token >= 256 ? 2 : 1;
+            const uint32_t length = cb.lengths[token];
+            if (!length) throw Error(NZ_ERUNTIME, "Symbol has no mixed codebook entry.");
+            const uint64_t code = cb.codes[token];
+            for (uint32_t done = 0; done < length;) {
+                const uint32_t take = std::min<uint32_t>(length - done, 32);
+                const uint64_t part = (code >> (length - done - take)) & ((uint64_t{1} << take) - 1);
+                acc = (acc << take) | part;
+                pending += take;
+                done += take;
+                while (pending >= 8) {
+                    pending -= 8;
+                    if (!put_byte(static_cast<uint8_t>(acc >> pending))) return 0;
+                    acc &= pending ? ((uint64_t{1} << pending) - 1) : 0;
+                }
+            }
+            bits += length;
+            ++tokens;
+        }
+        if (pending && !put_byte(static_cast<uint8_t>(acc << (8 - pending)))) return 0;
+        if (bits > 0xFFFFFFFFULL || tokens > 0xFFFFFFFFULL)
+            throw Error(NZ_ERUNTIME, "Mixed frame exceeds uint32 limits.");
+        if (out) {
+            for (int i = 0; i < 4; ++i) {
+                out[8 * lane + i] = static_cast<uint8_t>(tokens >> (8 * i));
+                out[8 * lane + 4 + i] = static_cast<uint8_t>(bits >> (8 * i));
+            }
+        }
+    }
+    return cursor;
+}
+
+// Forward MSB-first window: 64 bits starting at bit `at` of `stream`
+// (`bytes` long), zeros past the end.
+static inline uint64_t forward_window(const uint8_t* stream, uint64_t bytes, uint64_t at) {
+    const uint64_t byte = at >> 3;
+    uint64_t w = 0;
+    if (byte + 9 <= bytes) {
+        for (int i = 0; i < 8; ++i) w = (w << 8) | stream[byte + i];
+        const uint32_t sh = at & 7U;
+        if (sh) w = (w << sh) | (static_cast<uint64_t>(stream[byte + 8]) >> (8 - sh));
+        return w;
+    }
+    for (int i = 0; i < 9; ++i) {
+        const uint64_t b = byte + i < bytes ? stream[byte + i] : 0;
+        if (i < 8) w = (w << 8) | b;
+        else if (at & 7U) w = (w << (at & 7U)) | (b >> (8 - (at & 7U)));
+    }
+    return w;
+}
+
+// One token from a 64-bit window: writes its bytes (<= 2) and returns its
+// code length; 0 for an invalid prefix.
+static inline uint32_t decode_token(const Codebook& cb, uint64_t w, uint32_t* bytes, uint32_t* count) {
+    uint32_t e = cb.single[w >> 52];
+    if ((e >> 16) & 3U) {
+        *bytes = e & 0xFFFFU;
+        *count = (e >> 16) & 3U;
+        return e >> 20;
+    }
+    uint32_t node = e & (NZ_TREE_MAX_NODES - 1);
+    for (uint32_t used = NZ_LUT_BITS; used < NZ_MAX_CODE_BITS; ++used) {
+        const uint32_t child = cb.lut[NZ_LUT_ENTRIES + 2 * node + ((w >> (63 - used)) & 1U)];
+        if (child >> 28) {
+            *bytes = child & 0xFFFFU;
+            *count = (child >> 28) & 3U;
+            return used + 1;
+        }
+        node = child & (NZ_TREE_MAX_NODES - 1);
+    }
+    return 0;
+}
+
+void mixed_decode(const Codebook& cb, const uint8_t* data, uint64_t size, uint8_t* out, uint64_t expected) {
+    if (size < 32) throw Error(NZ_EVALUE, "Truncated mixed Huffman frame.");
+    auto read_u32 = [](const uint8_t* p) {
+        return static_cast<uint32_t>(p[0]) | (static_cast<uint32_t>(p[1]) << 8) |
+               (static_cast<uint32_t>(p[2]) << 16) | (static_cast<uint32_t>(p[3]) << 24);
+    };
+    uint64_t cursor = 32, written = 0;
+    for (unsigned lane = 0; lane < 4; ++lane) {
+        const uint32_t count = read_u32(data + 8 * lane);
+        const uint64_t bit_size = read_u32(data + 8 * lane + 4);
+        const uint64_t bytes = (bit_size + 7) / 8;
+        if (bytes > size - cursor || count > expected - written)
+            throw Error(NZ_EVALUE, "Mixed frame lengths exceed its payload.");
+        const uint8_t* stream = data + cursor;
+        uint64_t pos = 0;
+        for (uint32_t i = 0; i < count; ++i) {
+            uint32_t value = 0, n = 0;
+            const uint32_t length = decode_token(cb, forward_window(stream, bytes, pos), &value, &n);
+            if (!length) throw Error(NZ_EVALUE, "Invalid mixed Huffman prefix.");
+            if (pos + length > bit_size) throw Error(NZ_EVALUE, "Truncated mixed Huffman code.");
+            if (n > expected - written) throw Error(NZ_EVALUE, "Mixed expansion exceeds exponent count.");
+            out[written++] = static_cast<uint8_t>(value);
+            if (n == 2) out[written++] = static_cast<uint8_t>(value >> 8);
+            pos += length;
+        }
+        if (pos != bit_size) throw Error(NZ_EVALUE, "Mixed frame has unconsumed code bits.");
+        if (bit_size % 8 && (stream[bytes - 1] & ((1U << (8 - bit_size % 8)) - 1)))
+            throw Error(NZ_EVALUE, "Mixed frame has nonzero padding.");
+        cursor += bytes;
+    }
+    if (cursor != size || written != expected) throw Error(NZ_EVALUE, "Mixed decoded size mismatch.");
+}
+
+uint64_t huff0_encode(const Codebook& cb, const uint8_t* data, uint64_t size, uint8_t* out, uint64_t cap) {
+    if (size == 0 || size > 128 * 1024 || cap < 6 + 1 + 1 + 1 + 8) return 0;
+    for (uint64_t i = 0; i < size; ++i)
+        if (!cb.lengths[data[i]]) return 0;
+    const uint64_t segment = (size + 3) / 4;
+    uint64_t total = 6;
+    uint64_t sizes[4];
+    for (int s = 0; s < 4; ++s) {
+        const uint64_t begin = std::min<uint64_t>(size, segment * s);
+        const uint64_t end = s == 3 ? size : std::min<uint64_t>(size, segment * (s + 1));
+        if (begin >= end) return 0;
+        uint8_t* dst = out ? out + total : nullptr;
+        if (total >= cap) return 0;
+        BackwardWriter w{dst, cap - total};
+        for (uint64_t i = end; i-- > begin;) w.add(cb.codes[data[i]], cb.lengths[data[i]]);
+        w.close();
+        // A stream must leave 8 bytes of its capacity free (zstd's bit
+        // stream refuses to write its last container otherwise).
+        if (w.overflow || w.bytes + 8 > cap - total || w.bytes > 65535) return 0;
+        sizes[s] = w.bytes;
+        total += w.bytes;
+    }
+    if (out)
+        for (int s = 0; s < 3; ++s) {
+            out[2 * s] = static_cast<uint8_t>(sizes[s]);
+            out[2 * s + 1] = static_cast<uint8_t>(sizes[s] >> 8);
+        }
+    return total;
+}
+
+// Backward reader: `top` counts the unread bits below the end marker; the
+// next bits to read are [top - n, top) with bit top - 1 read first.
+static inline uint32_t backward_peek12(const uint8_t* stream, int64_t top) {
+    // Little-endian 64-bit word covering bits [8 * b0, 8 * b0 + 64).
+    const int64_t b0 = top >= 64 ? (top - 64 + 7) / 8 : 0;
+    uint64_t w = 0;
+    const int64_t last = (top + 7) / 8;  // bytes that hold unread bits
+    for (int64_t b = last - 1; b >= b0; --b) w = (w << 8) | stream[b];
+    const int64_t shift = top - 12 - 8 * b0;
+    if (shift >= 0) return static_cast<uint32_t>((w >> shift) & 0xFFFU);
+    return static_cast<uint32_t>((w << (-shift)) & 0xFFFU);
+}
+
+void huff0_decode(const Codebook& cb, const uint8_t* data, uint64_t size, uint8_t* out, uint64_t count) {
+    if (size < 10) throw Error(NZ_EVALUE, "Truncated Huff0 block.");
+    uint64_t sizes[4];
+    uint64_t sum = 0;
+    for (int s = 0; s < 3; ++s) {
+        sizes[s] = static_cast<uint64_t>(data[2 * s]) | (static_cast<uint64_t>(data[2 * s + 1]) << 8);
+        sum += sizes[s];
+    }
+    if (6 + sum >= size) throw Error(NZ_EVALUE, "Corrupt Huff0 jump table.");
+    sizes[3] = size - 6 - sum;
+    const uint64_t segment = (count + 3) / 4;
+    const uint8_t* stream = data + 6;
+    for (int s = 0; s < 4; ++s) {
+        const uint64_t begin = std::min<uint64_t>(count, segment * s);
+        const uint64_t end = s == 3 ? count : std::min<uint64_t>(count, segment * (s + 1));
+        const uint64_t n = sizes[s];
+        if (n == 0 || stream[n - 1] == 0) throw Error(NZ_EVALUE, "Corrupt Huff0 stream end.");
+        int64_t top = static_cast<int64_t>(8 * (n - 1) + (31 - __builtin_clz(stream[n - 1])));
+        for (uint64_t i = begin; i < end; ++i) {
+            const uint32_t e = cb.single[backward_peek12(stream, top)];
+            const uint32_t length = e >> 20;
+            if (!((e >> 16) & 3U) || top < static_cast<int64_t>(length))
+                throw Error(NZ_EVALUE, "Corrupt Huff0 stream.");
+            out[i] = static_cast<uint8_t>(e);
+            top -= length;
+        }
+        if (top != 0) throw Error(NZ_EVALUE, "Huff0 stream has unconsumed bits.");
+        stream += n;
+    }
+}
+
+}  // namespace nz
+
+using nz::Error;
+
+#define NZ_GUARD(...)                                    \
+    try {                                                \
+        __VA_ARGS__;                                     \
+        return NZ_OK;                                    \
+    } catch (const Error& e) {                           \
+        return nz::fail(e.status, e.what());             \
+    } catch (const std::exception& e) {                  \
+        return nz::fail(NZ_ERUNTIME, e.what());          \
+    }
+
+extern "C" {
+
+int nz_count_tokens(const uint8_t* data, uint64_t size, const uint8_t* vocab, uint32_t vocab_size,
+                    uint64_t* counts) {
+    NZ_GUARD({
+        if ((size && !data) || !counts || (vocab_size && !vocab)) throw Error(NZ_EVALUE, "Null argument.");
+        if (vocab_size % 2 || vocab_size > 2 * NZ_MAX_PAIRS) throw Error(NZ_EVALUE, "Invalid mixed pair vocabulary.");
+        std::vector<uint16_t> lookup(vocab_size ? 65536 : 0, 0);
+        for (uint32_t i = 0; i < vocab_size; i += 2) {
+            const uint32_t pair = vocab[i] | (vocab[i + 1] << 8);
+            if (lookup[pair]) throw Error(NZ_EVALUE, "Duplicate mixed pair definition.");
+            lookup[pair] = static_cast<uint16_t>(256 + i / 2);
+        }
+        for (uint64_t i = 0; i < size;) {
+            const uint32_t pair = vocab_size && i + 1 < size ? lookup[data[i] | (data[i + 1] << 8)] : 0;
+            ++counts[pair ? pair : data[i]];
+            i += pair ? 2 : 1;
+        }
+    })
+}
+
+int nz_exponent_histograms(const uint8_t* raw, uint64_t numel, const nz_dtype* dt, uint64_t step,
+                           uint64_t* histograms) {
+    NZ_GUARD({
+        if ((numel && !raw) || !dt || !histograms || step == 0) throw Error(NZ_EVALUE, "Null argument.");
+        nz::check_dtype(*dt);
+        const uint32_t mask = (1U << dt->exp_bits) - 1U;
+        for (uint64_t begin = 0, chunk = 0; begin < numel; begin += step, ++chunk) {
+            uint64_t* h = histograms + chunk * 256;
+            const uint64_t end = std::min(numel, begin + step);
+            if (dt->elem_size == 2) {
+                for (uint64_t i = begin; i < end; ++i) {
+                    uint16_t v;
+                    std::memcpy(&v, raw + 2 * i, 2);
+                    ++h[(v >> dt->mant_bits) & mask];
+                }
+            } else {
+                for (uint64_t i = begin; i < end; ++i) {
+                    uint32_t v;
+                    std::memcpy(&v, raw + 4 * i, 4);
+                    ++h[(v >> dt->mant_bits) & mask];
+                }
+            }
+        }
+    })
+}
+
+int nz_mixed_encode(const nz_codebook* codebook, const uint8_t* data, uint64_t size, uint8_t* out,
+                    uint64_t cap, uint64_t* written) {
+    NZ_GUARD({
+        if (!codebook || !written || (size && !data)) throw Error(NZ_EVALUE, "Null argument.");
+        *written = nz::mixed_encode(*reinterpret_cast<const nz::Codebook*>(codebook), data, size, out, cap);
+    })
+}
+
+int nz_mixed_decode(const nz_codebook* codebook, const uint8_t* frame, uint64_t size, uint8_t* out,
+                    uint64_t expected) {
+    NZ_GUARD({
+        if (!codebook || !frame || (expected && !out)) throw Error(NZ_EVALUE, "Null argument.");
+        nz::mixed_decode(*reinterpret_cast<const nz::Codebook*>(codebook), frame, size, out, expected);
+    })
+}
+
+int nz_huff0_encode(const nz_codebook* codebook, const uint8_t* data, uint64_t size, uint8_t* out,
+                    uint64_t cap, uint64_t* written) {
+    NZ_GUARD({
+        if (!codebook || !written || (size && !data)) throw Error(NZ_EVALUE, "Null argument.");
+        *written = nz::huff0_encode(*reinterpret_cast<const nz::Codebook*>(codebook), data, size, out, cap);
+    })
+}
+
+int nz_huff0_decode(const nz_codebook* codebook, const uint8_t* block, uint64_t size, uint8_t* out,
+                    uint64_t count) {
+    NZ_GUARD({
+        if (!codebook || !block || (count && !out)) throw Error(NZ_EVALUE, "Null argument.");
+        nz::huff0_decode(*reinterpret_cast<const nz::Codebook*>(codebook), block, size, out, count);
+    })
+}
+
+}  // extern "C"

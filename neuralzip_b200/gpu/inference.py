@@ -124,7 +124,7 @@ class GPUEncodedSymbols:
 class GPUEncoded:
     dtype: DTypeSpec
     numel: int
-    streams: tuple  # Indexed by byte-lane ID: bytes (raw) or GPUEncodedSymbols.
+    streams: tuple  # Indexed by byte-lane ID: raw lane bytes (bytes-like) or GPUEncodedSymbols.
 
     @property
     def raw_bytes(self):
@@ -132,7 +132,7 @@ class GPUEncoded:
 
     @property
     def compressed_bytes(self):
-        return sum(len(s) if isinstance(s, bytes) else s.compressed_bytes for s in self.streams)
+        return sum(s.compressed_bytes if isinstance(s, GPUEncodedSymbols) else len(s) for s in self.streams)
 
     @property
     def symbols(self):
@@ -178,9 +178,10 @@ def encode_gpu_native(raw, codebook_header, *, dtype, stream_id, vocab=b"", code
 
 def encode_raw_fragment(raw, *, dtype, stream_id):
     """Raw fragment: every lane stored as bytes, the selected one wrapped."""
-    lanes = _native.split_lanes(bytes(raw), _dtype_struct(dtype, stream_id))
+    raw = _as_bytes_array(raw)
+    lanes = _native.split_lanes(raw, _dtype_struct(dtype, stream_id))
     numel = len(raw) // dtype.element_size
-    streams = [lane.tobytes() for lane in lanes]
+    streams = [_view(lane) for lane in lanes]
     streams[stream_id] = GPUEncodedSymbols(streams[stream_id], 8 * numel, numel, b"", ())
     return GPUEncoded(dtype, numel, tuple(streams))
 
@@ -304,52 +305,122 @@ def _aligned(offset, element_size):
     return (offset + step - 1) // step * step
 
 
-def _assemble_export(block_order, candidates, compressor):
+def _view(array):
+    """Read-only byte view of a numpy array (no copy)."""
+    return memoryview(np.ascontiguousarray(array).view(np.uint8)).toreadonly()
+
+
+def _as_bytes_array(data):
+    if isinstance(data, np.ndarray):
+        return np.ascontiguousarray(data).reshape(-1).view(np.uint8)
+    return np.frombuffer(data, dtype=np.uint8)
+
+
+def _pack_parallel(items, threads=0):
+    """Packs (raw bytes, GPUCodebook, spec) items on the native thread pool
+    (nz_pack_many) and returns one GPUEncoded per item."""
+    results = [None] * len(items)
+    by_spec = defaultdict(list)
+    for index, (raw, book, spec) in enumerate(items):
+        by_spec[spec].append(index)
+    for spec, indices in by_spec.items():
+        dt = _dtype_struct(spec, spec.gpu_stream)
+        jobs, keep = [], []
+        for index in indices:
+            raw, book, _ = items[index]
+            raw_array = _as_bytes_array(raw)
+            numel = len(raw_array) // spec.element_size
+            words, n_lens, n_tiles = _native.pack_bound(numel, book.native.longest)
+            bits = np.empty(words, dtype=np.uint32)
+            lens = np.empty(n_lens, dtype=np.uint16)
+            tile_off = np.empty(n_tiles, dtype=np.uint32)
+            lanes = [None if lane == spec.gpu_stream else np.empty(numel, dtype=np.uint8)
+                     for lane in range(spec.element_size)]
+            job = _native.PackJob()
+            job.codebook = book.native.handle.value
+            job.raw = raw_array.ctypes.data if numel else None
+            job.numel = numel
+            job.bits, job.bits_cap_words = bits.ctypes.data, words
+            job.lens, job.lens_cap = lens.ctypes.data, n_lens
+            job.tile_off, job.tiles_cap = tile_off.ctypes.data, n_tiles
+            for lane in range(4):
+                job.lanes[lane] = lanes[lane].ctypes.data if lane < len(lanes) and lanes[lane] is not None else None
+            jobs.append(job)
+            keep.append((index, raw_array, bits, lens, tile_off, lanes, numel, book))
+        done = _native.pack_many(jobs, dt, threads)
+        for job, (index, _raw, bits, lens, tile_off, lanes, numel, book) in zip(done, keep):
+            streams = [_view(lane) if lane is not None else None for lane in lanes]
+            streams[spec.gpu_stream] = GPUEncodedSymbols(
+                _view(bits[:job.words_used]), int(job.bit_length), numel, _view(lens),
+                tuple(tile_off.tolist()))
+            results[index] = GPUEncoded(spec, numel, tuple(streams))
+    return results
+
+
+def _assemble(entries, compressor, threads=0):
     """One GPU group per source chunk (neuralzip/gpu/inference.py:288-336).
+    entries: (block_name, module_name, tensor_name, tensor) in export order.
     Tensor offsets inside a block workspace are rounded up to 128 bytes so
     every group's output is 16-byte aligned for the vector stores."""
     payloads = {int(p.codebook_id): p for p in compressor.export_codebooks()}
-    codebooks = {}
-    block_index = {name: index for index, name in enumerate(block_order)}
+    codebooks = {-1: GPUCodebook((), ())}
     workspace_offsets = defaultdict(int)
-    groups = []
-    for member in sorted(candidates, key=lambda c: (block_index[c.block_name], c.module_name)):
-        parameter = member.parameter
-        spec = DTYPES[parameter.dtype]
+    planned = []
+    for block_name, module_name, tensor_name, tensor in entries:
+        spec = DTYPES[tensor.dtype]
         stream_id = spec.gpu_stream
-        key = compressor._transfer_plan_key(member.tensor_name, parameter, stream_id)
-        modes = compressor._transfer_chunk_modes[key]
+        modes = compressor._transfer_chunk_modes[compressor._transfer_plan_key(tensor_name, tensor, stream_id)]
         step = _stream_chunk_size(compressor.chunk_size, spec.element_size)
-        raw = parameter.detach().cpu().contiguous().reshape(-1).view(torch.uint8).numpy().tobytes()
-        ws_key = (member.block_name, parameter.dtype)
-        workspace_offset = _aligned(workspace_offsets[ws_key], spec.element_size)
-        binding = LinearWeightBinding(member.module_name, member.tensor_name, tuple(parameter.shape),
-                                      parameter.numel(), workspace_offset)
-        fragments = []
+        raw = tensor.detach().cpu().contiguous().reshape(-1).view(torch.uint8).numpy()
+        chunks = []
         for chunk, mode in enumerate(modes):
             start = chunk * step
             part = raw[start * spec.element_size:(start + step) * spec.element_size]
             codebook_id = mode.get("codebook_id", -1) if mode.get("kind", "raw") != "raw" else -1
             if codebook_id not in codebooks:
-                if codebook_id == -1:
-                    codebooks[-1] = GPUCodebook((), ())
-                else:
-                    payload = payloads[codebook_id]
-                    codebooks[codebook_id] = codebook_from_header(bytes(payload.codebook), bytes(payload.vocab))
-            if codebook_id == -1:
-                encoded = encode_raw_fragment(part, dtype=spec, stream_id=stream_id)
-            else:
-                encoded = encode_with_codebook(part, codebooks[codebook_id], dtype=spec, stream_id=stream_id)
-            fragments.append(GPUWeightGroup(member.block_name, codebook_id, codebooks[codebook_id], encoded,
-                                            (binding,), workspace_offset + start))
+                payload = payloads[codebook_id]
+                codebooks[codebook_id] = codebook_from_header(bytes(payload.codebook), bytes(payload.vocab))
+            chunks.append((start, part, codebook_id))
+        planned.append((block_name, module_name, tensor_name, tensor, spec, raw, chunks))
+    coded = [(part, codebooks[cid], spec) for *_, spec, _raw, chunks in planned for _s, part, cid in chunks if cid != -1]
+    packed = iter(_pack_parallel(coded, threads))
+    groups = []
+    for block_name, module_name, tensor_name, tensor, spec, raw, chunks in planned:
+        ws_key = (block_name, tensor.dtype)
+        workspace_offset = _aligned(workspace_offsets[ws_key], spec.element_size)
+        binding = LinearWeightBinding(module_name, tensor_name, tuple(tensor.shape), tensor.numel(), workspace_offset)
+        fragments = []
+        for start, part, cid in chunks:
+            encoded = next(packed) if cid != -1 else encode_raw_fragment(part, dtype=spec, stream_id=spec.gpu_stream)
+            fragments.append(GPUWeightGroup(block_name, cid, codebooks[cid], encoded, (binding,),
+                                            workspace_offset + start))
         if sum(group.encoded.compressed_bytes for group in fragments) >= len(raw):
             continue
         groups.extend(fragments)
-        workspace_offsets[ws_key] = workspace_offset + parameter.numel()
+        workspace_offsets[ws_key] = workspace_offset + tensor.numel()
     return NeuralZipModelExport(tuple(groups))
 
 
-def export_model_for_gpu(model, setup, *, allowed_dtypes=DTYPES):
+def _assemble_export(block_order, candidates, compressor, threads=0):
+    block_index = {name: index for index, name in enumerate(block_order)}
+    ordered = sorted(candidates, key=lambda c: (block_index[c.block_name], c.module_name))
+    return _assemble([(c.block_name, c.module_name, c.tensor_name, c.parameter) for c in ordered], compressor,
+                     threads)
+
+
+def export_tensors_for_gpu(named_tensors, setup, *, block_name="tensors", threads=0):
+    """Exports a mapping of floating tensors as one block (bulk decode, no
+    model): every tensor is bound under its own name."""
+    from neuralzip_b200.compressor import NeuralZipCompressor
+
+    items = [(str(name), tensor) for name, tensor in dict(named_tensors).items()
+             if torch.is_tensor(tensor) and tensor.dtype in DTYPES and tensor.numel()]
+    compressor = NeuralZipCompressor(setup, gpu=True)
+    compressor.prepare_gpu_transfer_target(items)
+    return _assemble([(block_name, name, name, tensor) for name, tensor in items], compressor, threads)
+
+
+def export_model_for_gpu(model, setup, *, allowed_dtypes=DTYPES, threads=0):
     """Exports the frozen chunk tables, including adaptive singleton/pair
     codes (neuralzip/gpu/inference.py:339-358)."""
     from neuralzip_b200.compressor import NeuralZipCompressor
@@ -364,7 +435,7 @@ def export_model_for_gpu(model, setup, *, allowed_dtypes=DTYPES):
         return NeuralZipModelExport(())
     compressor = NeuralZipCompressor(setup, gpu=True)
     compressor.prepare_gpu_transfer_target(tuple((c.tensor_name, c.parameter) for c in candidates))
-    return _assemble_export(blocks, candidates, compressor)
+    return _assemble_export(blocks, candidates, compressor, threads)
 
 
 def _binding_module(model, binding):

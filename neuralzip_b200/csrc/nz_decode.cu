@@ -31,78 +31,91 @@
 
 namespace {
 
-constexpr uint32_t kRoundElems = 64;                       // per lane per staging round
-constexpr uint32_t kRounds = NZ_LANE_ELEMS / kRoundElems;  // 4
-constexpr uint32_t kStageStride = kRoundElems / 4 + 1;     // words per staged row
+constexpr uint32_t kRoundElems = 128;                      // per lane per staging round
+constexpr uint32_t kRounds = NZ_LANE_ELEMS / kRoundElems;  // 2
+constexpr uint32_t kStageStride = kRoundElems / 4 + 1;     // words per staged row (odd: no conflicts)
 constexpr uint32_t kStageWordsPerWarp = NZ_TILE_LANES * kStageStride;
+constexpr uint32_t kLanesPerRow = kRoundElems / 8;          // merge: 8 elements per lane
+constexpr uint32_t kRowsPerPass = 32 / kLanesPerRow;
+constexpr uint32_t kMergePasses = NZ_TILE_LANES / kRowsPerPass;
 constexpr uint32_t kTreeMask = NZ_TREE_MAX_NODES - 1;
 constexpr uint32_t kMaxTreeDepth = NZ_MAX_CODE_BITS - NZ_LUT_BITS;
 constexpr int32_t kStatusCorruptTable = 2;
 
-__device__ __forceinline__ uint32_t ldg_u32(const uint32_t* p) { return __ldg(p); }
-
-__device__ __forceinline__ uint2 ldg_stream_u2(const void* p) {
-    uint2 v;
-    asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0, %1}, [%2];"
-                 : "=r"(v.x), "=r"(v.y)
-                 : "l"(p));
-    return v;
+__device__ __forceinline__ uint2 ldg_u2(const void* p) {
+    return __ldg(reinterpret_cast<const uint2*>(p));
 }
 
 __device__ __forceinline__ void stg_u4(void* p, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
-    asm volatile("st.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(a), "r"(b), "r"(c),
-                 "r"(d)
-                 : "memory");
+    *reinterpret_cast<uint4*>(p) = make_uint4(a, b, c, d);
 }
 
-// MSB-first reader over 32-bit words (bit 31 earliest) with one word of
-// prefetch; `buf` holds `nvalid` valid bits left-aligned.
-struct BitReader {
-    uint64_t buf;
-    uint32_t nvalid;
-    uint32_t pf;
-    const uint32_t* ptr;
+// MSB-first window over 32-bit words (bit 31 earliest). The valid bits are
+// the top `avail` bits of hi:lo and everything below them is zero. One word
+// is prefetched. All shifts are 32-bit funnel shifts.
+struct Window {
+    uint32_t hi, lo, avail, pf;
+    const uint32_t* src;
 
     __device__ __forceinline__ void init(const uint32_t* words, uint32_t bitpos) {
         const uint32_t* p = words + (bitpos >> 5);
         const uint32_t sh = bitpos & 31U;
-        const uint64_t w = (static_cast<uint64_t>(ldg_u32(p)) << 32) | ldg_u32(p + 1);
-        buf = w << sh;
-        nvalid = 64U - sh;
-        ptr = p + 2;
-        pf = ldg_u32(ptr);
+        const uint32_t w0 = __ldg(p), w1 = __ldg(p + 1);
+        hi = __funnelshift_l(w1, w0, sh);
+        lo = w1 << sh;
+        avail = 64U - sh;
+        src = p + 2;
+        pf = __ldg(src);
     }
-    // Precondition: nvalid <= 32.
-    __device__ __forceinline__ void refill() {
-        buf |= static_cast<uint64_t>(pf) << (32U - nvalid);
-        nvalid += 32U;
-        ++ptr;
-        pf = ldg_u32(ptr);
-    }
+    // Drops n (< 32) bits; only the low five bits of n are used.
     __device__ __forceinline__ void consume(uint32_t n) {
-        buf <<= n;
-        nvalid -= n;
+        hi = __funnelshift_l(lo, hi, n);
+        lo = __funnelshift_l(0U, lo, n);
+        avail -= n & 31U;
+    }
+    // Appends the prefetched word when at most 32 bits remain.
+    __device__ __forceinline__ void top_up() {
+        if (avail <= 32U) {
+            hi |= __funnelshift_rc(pf, 0U, avail);
+            lo = __funnelshift_rc(0U, pf, avail);
+            avail += 32U;
+            pf = __ldg(++src);
+        }
     }
 };
 
-// Walks the suffix tree for a code longer than 12 bits. `marker` is the LUT
-// entry (node index reached after the first 12 bits). Returns a leaf entry
-// (bytes | count << 28). The depth is bounded by 44; a table that exceeds
-// it sets *status and yields one zero byte so the lane still terminates.
+// Code longer than 12 bits: consume the 12-bit prefix, then walk the suffix
+// tree one bit at a time (at most 44 steps). Returns a leaf word (byte
+// count in bits 5..6, bytes in 8..23, zero shift). A table that exceeds the
+// depth sets *status and yields one zero byte, so the lane still finishes.
 __device__ __forceinline__ uint32_t walk_long(const uint32_t* __restrict__ table, uint32_t marker,
-                                            BitReader& br, int32_t* status) {
-    br.consume(NZ_LUT_BITS);
-    uint32_t node = marker & kTreeMask;
+                                            uint32_t& hi, uint32_t& lo, uint32_t& avail, uint32_t& pf,
+                                            const uint32_t*& src, int32_t* status) {
+    Window w{hi, lo, avail, pf, src};
+    w.consume(NZ_LUT_BITS);
+    uint32_t node = (marker >> 8) & kTreeMask;
+    uint32_t leaf = 0;
     for (uint32_t d = 0; d < kMaxTreeDepth; ++d) {
-        if (br.nvalid <= 32U) br.refill();
-        const uint32_t bit = static_cast<uint32_t>(br.buf >> 63);
-        br.consume(1);
+        w.top_up();
+        const uint32_t bit = w.hi >> 31;
+        w.consume(1);
         const uint32_t child = table[NZ_LUT_ENTRIES + 2U * node + bit];
-        if (child >> 28) return child;
-        node = child & kTreeMask;
+        if (child & 0x60U) {
+            leaf = child & ~0x1FU;
+            break;
+        }
+        node = (child >> 8) & kTreeMask;
     }
-    if (status) *status = kStatusCorruptTable;
-    return 1U << 28;
+    if (!leaf) {
+        if (status) *status = kStatusCorruptTable;
+        leaf = 1U << 5;
+    }
+    hi = w.hi;
+    lo = w.lo;
+    avail = w.avail;
+    pf = w.pf;
+    src = w.src;
+    return leaf;
 }
 
 // Element assembly (undoes DTypeSpec.reorder_bytes, neuralzip/dtypes.py:
@@ -114,20 +127,20 @@ struct Layout;
 template <bool REORDER>
 struct Layout<2, REORDER> {
     static constexpr int kSel = 1;
-    // Two elements: raw bytes r (low 16 bits used), decoded bytes x.
+    static constexpr int kRawLanes = 1;
     __device__ __forceinline__ static uint32_t pair(uint32_t r, uint32_t x, uint32_t sel) {
         const uint32_t t = __byte_perm(r, x, sel);
         if (!REORDER) return t;
         return (t & 0x007F007FU) | ((t >> 1) & 0x7F807F80U) | ((t << 8) & 0x80008000U);
     }
-    __device__ __forceinline__ static void store8(uint8_t* out, const uint8_t* const* lanes,
-                                                  uint32_t e, uint32_t x0, uint32_t x1) {
-        const uint2 r = ldg_stream_u2(lanes[0] + e);
-        stg_u4(out + 2ull * e, pair(r.x, x0, 0x5140), pair(r.x, x0, 0x7362),
-               pair(r.y, x1, 0x5140), pair(r.y, x1, 0x7362));
+    // 8 elements from raw bytes r[0] (lane 0) and decoded bytes x0, x1.
+    __device__ __forceinline__ static void store8(uint8_t* out, uint32_t e, const uint2* r, uint32_t x0,
+                                                  uint32_t x1) {
+        stg_u4(out + 2ull * e, pair(r[0].x, x0, 0x5140), pair(r[0].x, x0, 0x7362), pair(r[0].y, x1, 0x5140),
+               pair(r[0].y, x1, 0x7362));
     }
-    __device__ __forceinline__ static void store1(uint8_t* out, const uint8_t* const* lanes,
-                                                  uint32_t e, uint32_t x) {
+    __device__ __forceinline__ static void store1(uint8_t* out, const uint8_t* const* lanes, uint32_t e,
+                                                  uint32_t x) {
         uint32_t v = static_cast<uint32_t>(lanes[0][e]) | (x << 8);
         if (REORDER) v = (v & 0x7FU) | ((v >> 1) & 0x7F80U) | ((v << 8) & 0x8000U);
         reinterpret_cast<uint16_t*>(out)[e] = static_cast<uint16_t>(v);
@@ -138,49 +151,40 @@ struct Layout<2, REORDER> {
 template <>
 struct Layout<4, true> {
     static constexpr int kSel = 3;
+    static constexpr int kRawLanes = 3;
     __device__ __forceinline__ static uint32_t fix(uint32_t v) {
         return (v & 0x007FFFFFU) | ((v >> 1) & 0x7F800000U) | ((v << 8) & 0x80000000U);
     }
-    __device__ __forceinline__ static uint32_t word(uint32_t l0, uint32_t l1, uint32_t l2,
-                                                    uint32_t x, uint32_t i) {
+    __device__ __forceinline__ static uint32_t word(uint32_t l0, uint32_t l1, uint32_t l2, uint32_t x,
+                                                    uint32_t i) {
         const uint32_t lo = __byte_perm(l0, l1, i | ((i + 4U) << 4));
         const uint32_t hi = __byte_perm(l2, x, i | ((i + 4U) << 4));
         return fix(__byte_perm(lo, hi, 0x5410));
     }
-    __device__ __forceinline__ static void store8(uint8_t* out, const uint8_t* const* lanes,
-                                                  uint32_t e, uint32_t x0, uint32_t x1) {
-        const uint2 a = ldg_stream_u2(lanes[0] + e);
-        const uint2 b = ldg_stream_u2(lanes[1] + e);
-        const uint2 c = ldg_stream_u2(lanes[2] + e);
+    __device__ __forceinline__ static void store8(uint8_t* out, uint32_t e, const uint2* r, uint32_t x0,
+                                                  uint32_t x1) {
         uint8_t* o = out + 4ull * e;
-        stg_u4(o, word(a.x, b.x, c.x, x0, 0), word(a.x, b.x, c.x, x0, 1),
-               word(a.x, b.x, c.x, x0, 2), word(a.x, b.x, c.x, x0, 3));
-        stg_u4(o + 16, word(a.y, b.y, c.y, x1, 0), word(a.y, b.y, c.y, x1, 1),
-               word(a.y, b.y, c.y, x1, 2), word(a.y, b.y, c.y, x1, 3));
+        stg_u4(o, word(r[0].x, r[1].x, r[2].x, x0, 0), word(r[0].x, r[1].x, r[2].x, x0, 1),
+               word(r[0].x, r[1].x, r[2].x, x0, 2), word(r[0].x, r[1].x, r[2].x, x0, 3));
+        stg_u4(o + 16, word(r[0].y, r[1].y, r[2].y, x1, 0), word(r[0].y, r[1].y, r[2].y, x1, 1),
+               word(r[0].y, r[1].y, r[2].y, x1, 2), word(r[0].y, r[1].y, r[2].y, x1, 3));
     }
-    __device__ __forceinline__ static void store1(uint8_t* out, const uint8_t* const* lanes,
-                                                  uint32_t e, uint32_t x) {
-        const uint32_t v = static_cast<uint32_t>(lanes[0][e]) |
-                           (static_cast<uint32_t>(lanes[1][e]) << 8) |
+    __device__ __forceinline__ static void store1(uint8_t* out, const uint8_t* const* lanes, uint32_t e,
+                                                  uint32_t x) {
+        const uint32_t v = static_cast<uint32_t>(lanes[0][e]) | (static_cast<uint32_t>(lanes[1][e]) << 8) |
                            (static_cast<uint32_t>(lanes[2][e]) << 16) | (x << 24);
         reinterpret_cast<uint32_t*>(out)[e] = fix(v);
     }
 };
 
-// Merges 8 consecutive elements starting at e (< numel) whose decoded
-// bytes are x0 (elements e..e+3) and x1 (e+4..e+7).
+// Scalar tail: elements e .. min(e + 8, numel) with decoded bytes x0 | x1.
 template <int ES, bool REORDER>
-__device__ __forceinline__ void merge8(uint8_t* out, const uint8_t* const* lanes, bool vec_ok,
-                                       uint32_t e, uint32_t numel, uint32_t x0, uint32_t x1) {
-    using L = Layout<ES, REORDER>;
-    if (vec_ok && e + 8U <= numel) {
-        L::store8(out, lanes, e, x0, x1);
-        return;
-    }
+__device__ __forceinline__ void merge_tail(uint8_t* out, const uint8_t* const* lanes, uint32_t e, uint32_t numel,
+                                           uint32_t x0, uint32_t x1) {
     const uint32_t n = min(8U, numel - e);
     for (uint32_t j = 0; j < n; ++j) {
         const uint32_t x = ((j < 4 ? x0 : x1) >> (8U * (j & 3U))) & 0xFFU;
-        L::store1(out, lanes, e + j, x);
+        Layout<ES, REORDER>::store1(out, lanes, e + j, x);
     }
 }
 
@@ -189,6 +193,7 @@ __global__ void __launch_bounds__(NW * 32, (NW >= 16 ? 2 : (NW >= 8 ? 4 : 8)))
     nz_tile_decode(const nz_group* __restrict__ groups, const nz_work* __restrict__ works,
                    const nz_cta* __restrict__ ctas, const uint64_t* __restrict__ luts,
                    int32_t* __restrict__ status) {
+    using L = Layout<ES, REORDER>;
     extern __shared__ __align__(16) uint32_t smem[];
     uint32_t* table = smem;
     const uint32_t warp = threadIdx.x >> 5;
@@ -196,8 +201,7 @@ __global__ void __launch_bounds__(NW * 32, (NW >= 16 ? 2 : (NW >= 8 ? 4 : 8)))
     uint32_t* stage = smem + NZ_LUT_WORDS + warp * kStageWordsPerWarp;
 
     const nz_cta cta = ctas[blockIdx.x];
-    const bool coded = cta.lut != NZ_RAW_LUT;
-    if (coded) {
+    if (cta.lut != NZ_RAW_LUT) {
         const uint4* src = reinterpret_cast<const uint4*>(luts[cta.lut]);
         uint4* dst = reinterpret_cast<uint4*>(table);
         const uint32_t n4 = (min(cta.lut_words, NZ_LUT_WORDS) + 3U) / 4U;  // tables hold NZ_LUT_WORDS
@@ -215,33 +219,33 @@ __global__ void __launch_bounds__(NW * 32, (NW >= 16 ? 2 : (NW >= 8 ? 4 : 8)))
         for (int l = 0; l < 4; ++l) lanes[l] = reinterpret_cast<const uint8_t*>(g.lanes[l]);
         uint64_t align = g.out;
 #pragma unroll
-        for (int l = 0; l < ES; ++l)
-            if (l != Layout<ES, REORDER>::kSel) align |= g.lanes[l];
+        for (int l = 0; l < L::kRawLanes; ++l) align |= g.lanes[l];
         const bool vec_ok = (align & 15U) == 0;
         const uint32_t tile_base = item.tile * NZ_TILE_ELEMS;
 
         if (g.lut == NZ_RAW_LUT) {
             // Raw fragment: the selected lane is stored as bytes.
-            const uint8_t* sel = lanes[Layout<ES, REORDER>::kSel];
-            const bool sel_ok = vec_ok && (reinterpret_cast<uint64_t>(sel) & 7U) == 0;
+            const uint8_t* sel = lanes[L::kSel];
+            const bool sel_ok = vec_ok && (reinterpret_cast<uint64_t>(sel) & 15U) == 0;
             for (uint32_t it = 0; it < NZ_TILE_ELEMS / 256; ++it) {
                 const uint32_t e = tile_base + it * 256U + lane * 8U;
                 if (e >= numel) break;
-                uint32_t x0, x1;
                 if (sel_ok && e + 8U <= numel) {
-                    const uint2 x = ldg_stream_u2(sel + e);
-                    x0 = x.x;
-                    x1 = x.y;
+                    const uint2 x = ldg_u2(sel + e);
+                    uint2 r[L::kRawLanes];
+#pragma unroll
+                    for (int l = 0; l < L::kRawLanes; ++l) r[l] = ldg_u2(lanes[l] + e);
+                    L::store8(out, e, r, x.x, x.y);
                 } else {
-                    x0 = x1 = 0;
+                    uint32_t x0 = 0, x1 = 0;
                     const uint32_t n = min(8U, numel - e);
                     for (uint32_t j = 0; j < n; ++j) {
                         const uint32_t b = sel[e + j];
                         if (j < 4) x0 |= b << (8U * j);
                         else x1 |= b << (8U * (j - 4U));
                     }
+                    merge_tail<ES, REORDER>(out, lanes, e, numel, x0, x1);
                 }
-                merge8<ES, REORDER>(out, lanes, sel_ok, e, numel, x0, x1);
             }
             continue;
         }
@@ -257,11 +261,11 @@ __global__ void __launch_bounds__(NW * 32, (NW >= 16 ? 2 : (NW >= 8 ? 4 : 8)))
             const uint32_t v = __shfl_up_sync(0xFFFFFFFFU, incl, d);
             if (lane >= d) incl += v;
         }
-        const uint32_t start = reinterpret_cast<const uint32_t*>(g.tile_off)[item.tile] + incl - len;
-        BitReader br;
-        br.init(reinterpret_cast<const uint32_t*>(g.bits), start);
-        uint64_t q = 0;
-        uint32_t qn = 0, pushed = 0;
+        Window win;
+        win.init(reinterpret_cast<const uint32_t*>(g.bits),
+                 reinterpret_cast<const uint32_t*>(g.tile_off)[item.tile] + incl - len);
+        // Byte queue qb:qa, `qbits` bits queued (< 32 between iterations).
+        uint32_t qa = 0, qb = 0, qbits = 0;
         uint32_t* row = stage + lane * kStageStride;
 
         for (uint32_t r = 0; r < kRounds; ++r) {
@@ -270,36 +274,49 @@ __global__ void __launch_bounds__(NW * 32, (NW >= 16 ? 2 : (NW >= 8 ? 4 : 8)))
             const uint32_t want = n_lane > done ? min(kRoundElems, n_lane - done) : 0U;
             const uint32_t target = (want + 3U) >> 2;
             for (uint32_t wi = 0; wi < target;) {
-                if (pushed < n_lane) {
-                    uint32_t e = table[static_cast<uint32_t>(br.buf >> (64 - NZ_LUT_BITS))];
-                    uint32_t nbits = (e >> 24) & 15U;
-                    if ((e >> 28) == 0) {
-                        e = walk_long(table, e, br, status);
-                        nbits = 0;
-                    }
-                    const uint32_t nb = (e >> 28) & 3U;
-                    q |= static_cast<uint64_t>(e & 0xFFFFFFU) << (8U * qn);
-                    qn += nb;
-                    pushed += nb;
-                    br.consume(nbits);
-                    if (br.nvalid <= 32U) br.refill();
-                }
-                if (qn >= 4U || pushed >= n_lane) {
-                    row[wi++] = static_cast<uint32_t>(q);
-                    q >>= 32;
-                    qn = qn >= 4U ? qn - 4U : 0U;
+                uint32_t e = table[win.hi >> (32 - NZ_LUT_BITS)];
+                if ((e & 0x60U) == 0U)
+                    e = walk_long(table, e, win.hi, win.lo, win.avail, win.pf, win.src, status);
+                win.consume(e);
+                win.top_up();
+                const uint32_t x = e >> 8;
+                qa |= x << qbits;
+                qb |= __funnelshift_l(x, 0U, qbits);
+                qbits += (e >> 2) & 0x18U;
+                if (qbits >= 32U) {
+                    row[wi++] = qa;
+                    qa = qb;
+                    qb = 0;
+                    qbits -= 32U;
                 }
             }
             __syncwarp();
-            // Merge the 32 staged rows: 8 lanes per row, 8 elements per lane.
-#pragma unroll 2
-            for (uint32_t it = 0; it < NZ_TILE_LANES / 4; ++it) {
-                const uint32_t rrow = it * 4U + (lane >> 3);
-                const uint32_t col = (lane & 7U) * 8U;
-                const uint32_t e = tile_base + rrow * NZ_LANE_ELEMS + done + col;
-                if (e < numel) {
+            // Merge the 32 staged rows: kLanesPerRow lanes per row, 8
+            // elements per lane; loads of a group of passes are issued first.
+            const uint32_t col = (lane % kLanesPerRow) * 8U;
+            constexpr uint32_t kGroup = ES == 4 ? 2 : 4;
+#pragma unroll
+            for (uint32_t p0 = 0; p0 < kMergePasses; p0 += kGroup) {
+                uint2 raw[kGroup][L::kRawLanes];
+                uint32_t ex[kGroup];
+                bool full[kGroup];
+#pragma unroll
+                for (uint32_t k = 0; k < kGroup; ++k) {
+                    const uint32_t rrow = (p0 + k) * kRowsPerPass + lane / kLanesPerRow;
+                    ex[k] = tile_base + rrow * NZ_LANE_ELEMS + done + col;
+                    full[k] = vec_ok && ex[k] + 8U <= numel;
+                    if (full[k]) {
+#pragma unroll
+                        for (int l = 0; l < L::kRawLanes; ++l) raw[k][l] = ldg_u2(lanes[l] + ex[k]);
+                    }
+                }
+#pragma unroll
+                for (uint32_t k = 0; k < kGroup; ++k) {
+                    const uint32_t rrow = (p0 + k) * kRowsPerPass + lane / kLanesPerRow;
                     const uint32_t* src = stage + rrow * kStageStride + (col >> 2);
-                    merge8<ES, REORDER>(out, lanes, vec_ok, e, numel, src[0], src[1]);
+                    const uint32_t x0 = src[0], x1 = src[1];
+                    if (full[k]) L::store8(out, ex[k], raw[k], x0, x1);
+                    else if (ex[k] < numel) merge_tail<ES, REORDER>(out, lanes, ex[k], numel, x0, x1);
                 }
             }
             __syncwarp();

@@ -118,14 +118,16 @@ std::vector<uint64_t> canonical_mixed_codes(const uint8_t* lengths, uint32_t nsy
 }
 
 // Multi-symbol decode table. Entry for a 12-bit window:
-//   bits  0..23  up to three decoded bytes (first byte lowest)
-//   bits 24..27  window bits those tokens consume (1..12)
-//   bits 28..29  number of decoded bytes (1..3)
+//   bits  0..3   window bits the decoded tokens consume (1..12); bit 4 is
+//                zero so the low five bits are directly a shift amount
+//   bits  5..6   number of decoded bytes (1..3)
+//   bits  8..31  up to three decoded bytes (first byte lowest)
 // A window whose first code is longer than 12 bits holds instead the index
-// of the trie node reached after 12 bits, with a zero byte count; the
-// kernel then walks the suffix tree stored after the 4096 entries, two
-// words per node (child for bit 0, child for bit 1), where a child with a
-// nonzero byte count is a leaf (bytes in bits 0..15).
+// of the trie node reached after 12 bits (bits 8..31) with a zero byte
+// count; the kernel then walks the suffix tree stored after the 4096
+// entries, two words per node (child for bit 0, child for bit 1), where a
+// child with a nonzero byte count is a leaf (bytes in bits 8..23) and any
+// other child holds the next node index in bits 8..31.
 void Codebook::build_lut() {
     std::vector<TrieNode> trie(1);
     for (uint32_t s = 0; s < nsym; ++s) {
@@ -214,7 +216,7 @@ void Codebook::build_lut() {
                     throw Error(NZ_EVALUE, "The Huffman codebook does not cover every prefix.");
             }
             if (trie[node].symbol < 0) {
-                if (pos == 0) entry = static_cast<uint32_t>(trie[node].suffix);
+                if (pos == 0) entry = static_cast<uint32_t>(trie[node].suffix) << 8;
                 break;
             }
             uint32_t value = 0;
@@ -224,7 +226,7 @@ void Codebook::build_lut() {
             nbytes += count;
             pos += depth;
         }
-        if (nbytes) entry = bytes | (pos << 24) | (nbytes << 28);
+        if (nbytes) entry = (bytes << 8) | pos | (nbytes << 5);
         lut[prefix] = entry;
     }
     // Suffix tree below depth 12.
@@ -240,9 +242,10 @@ void Codebook::build_lut() {
                 uint32_t value = 0;
                 const uint32_t count = token_bytes(trie[child].symbol, &value);
                 const uint32_t length = lengths[static_cast<size_t>(trie[child].symbol)];
-                word = value | ((length & 15U) << 24) | (count << 28);
+                (void)length;
+                word = (value << 8) | (count << 5);
             } else {
-                word = static_cast<uint32_t>(trie[child].suffix);
+                word = static_cast<uint32_t>(trie[child].suffix) << 8;
             }
             lut[NZ_LUT_ENTRIES + 2 * static_cast<uint32_t>(node.suffix) + b] = word;
         }

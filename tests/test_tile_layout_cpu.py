@@ -28,7 +28,8 @@ def _roundtrip(raw, spec, book, model=True):
     got = O.tile_decode(bits, lens, tile_off, enc.numel, book.code_lengths, book.code_values, book.vocab)
     assert np.array_equal(got, expected)
     if model:
-        modeled = KM.decode_group(np.asarray(book.decode_lut), bits, lens, tile_off, enc.numel)
+        modeled = KM.decode_group(np.asarray(book.decode_lut), bits, lens, tile_off, enc.numel,
+                                  lut_words=book.table_words)
         assert np.array_equal(modeled, expected)
     lanes = O.split(raw, spec)
     for lane, data in enumerate(enc.streams):
@@ -71,10 +72,8 @@ def test_gaussian_singleton_and_mixed(dtype):
 
 
 def test_pairs_never_straddle_substreams():
-    # A pair token of (7, 7) everywhere: positions 255|256 must not pair.
-    lengths = bytearray([9] * 256 + [1])
-    lengths[7] = 2
-    # make the code complete: 1 (pair) + 1/4 (sym 7) + 255 * 2^-9 ... adjust with canonical builder
+    # The pair (7, 7) everywhere: elements 255 and 256 of a group must not
+    # form a pair, since they belong to different sub-streams.
     counts = [1] * 256 + [10_000]
     counts[7] = 1000
     lengths = H.huffman_lengths_heap(counts)

@@ -19,8 +19,10 @@
  * as 32-bit words whose bit 31 is the earliest bit. `lens[s]` holds the bit
  * length of sub-stream s and `tile_off[t]` the bit offset of tile t's first
  * sub-stream; a lane finds its start with a warp scan of its tile's lens.
- * A pair token never straddles two sub-streams. The non-selected byte lanes
- * are stored raw, one byte per element, 16-byte aligned.
+ * A pair token never straddles two sub-streams. The bitstream starts on a
+ * 16-byte boundary and ends with at least NZ_BITS_PAD_WORDS zero words (the
+ * kernel reads ahead in 16-byte blocks). The non-selected byte lanes are
+ * stored raw, one byte per element, 16-byte aligned.
  */
 #ifndef NZ_B200_H
 #define NZ_B200_H
@@ -38,11 +40,12 @@ extern "C" {
 #define NZ_LUT_BITS 12u
 #define NZ_LUT_ENTRIES (1u << NZ_LUT_BITS)
 #define NZ_TREE_MAX_NODES 512u
-#define NZ_LUT_WORDS (NZ_LUT_ENTRIES + 2u * NZ_TREE_MAX_NODES)
+#define NZ_LUT_TREE (2u * NZ_LUT_ENTRIES)
+#define NZ_LUT_WORDS (NZ_LUT_TREE + 2u * NZ_TREE_MAX_NODES)
 #define NZ_MAX_CODE_BITS 56u
 #define NZ_MAX_SINGLETON_BITS 12u
 #define NZ_MAX_PAIRS 254u
-#define NZ_BITS_PAD_WORDS 8u
+#define NZ_BITS_PAD_WORDS 16u
 #define NZ_RAW_LUT 0xFFFFFFFFu
 
 enum nz_status {

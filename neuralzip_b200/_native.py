@@ -14,7 +14,10 @@ from pathlib import Path
 
 import numpy as np
 
-LIBRARY = Path(__file__).resolve().parent / "_lib" / "libnzb200.so"
+import os
+
+# NZB200_LIBRARY may point at another build of the same ABI (e.g. a debug build).
+LIBRARY = Path(os.environ.get("NZB200_LIBRARY") or Path(__file__).resolve().parent / "_lib" / "libnzb200.so")
 
 LANE_ELEMS = 256
 TILE_LANES = 32
@@ -22,9 +25,10 @@ TILE_ELEMS = LANE_ELEMS * TILE_LANES
 LUT_BITS = 12
 LUT_ENTRIES = 1 << LUT_BITS
 TREE_MAX_NODES = 512
-LUT_WORDS = LUT_ENTRIES + 2 * TREE_MAX_NODES
+LUT_TREE = 2 * LUT_ENTRIES
+LUT_WORDS = LUT_TREE + 2 * TREE_MAX_NODES
 MAX_CODE_BITS = 56
-BITS_PAD_WORDS = 8
+BITS_PAD_WORDS = 16
 RAW_LUT = 0xFFFFFFFF
 
 OK, EVALUE, ETYPE, EOVERFLOW, ERUNTIME, ECUDA = range(6)

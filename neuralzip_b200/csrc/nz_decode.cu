@@ -13,8 +13,9 @@
 //     decodes every segment twice and scans with two block barriers,
 //     decode.cu:129-175, 207-255);
 //   * the decode table lives in shared memory (staged once per CTA) and one
-//     lookup of the 12-bit window yields up to three output bytes; codes of
-//     13..56 bits continue through a suffix tree in the same table
+//     8-byte lookup of the 12-bit window yields up to four output bytes (two
+//     pair tokens); codes of 13..56 bits continue through a suffix tree in
+//     the same table
 //     (decode.cu:41-60 reads its table through __ldg, one token per probe);
 //   * decoded bytes are staged per warp, 64 elements per lane at a time, and
 //     merged with the raw lanes through 8-byte loads and 16-byte stores that
@@ -42,8 +43,11 @@ constexpr uint32_t kTreeMask = NZ_TREE_MAX_NODES - 1;
 constexpr uint32_t kMaxTreeDepth = NZ_MAX_CODE_BITS - NZ_LUT_BITS;
 constexpr int32_t kStatusCorruptTable = 2;
 
+// Streaming 8-byte load of a raw lane: read once, kept out of L1.
 __device__ __forceinline__ uint2 ldg_u2(const void* p) {
-    return __ldg(reinterpret_cast<const uint2*>(p));
+    uint2 v;
+    asm("ld.global.nc.L1::no_allocate.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
+    return v;
 }
 
 __device__ __forceinline__ void stg_u4(void* p, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
@@ -51,21 +55,23 @@ __device__ __forceinline__ void stg_u4(void* p, uint32_t a, uint32_t b, uint32_t
 }
 
 // MSB-first window over 32-bit words (bit 31 earliest). The valid bits are
-// the top `avail` bits of hi:lo and everything below them is zero. One word
-// is prefetched. All shifts are 32-bit funnel shifts.
+// the top `avail` bits of hi:lo and everything below them is zero. The next
+// word is requested one refill ahead (pf); a deeper queue of registers does
+// not help, since moving a pending load's register waits for the load. All
+// shifts are 32-bit funnel shifts.
 struct Window {
     uint32_t hi, lo, avail, pf;
-    const uint32_t* src;
+    const uint32_t* src;  // next word to request
 
     __device__ __forceinline__ void init(const uint32_t* words, uint32_t bitpos) {
         const uint32_t* p = words + (bitpos >> 5);
         const uint32_t sh = bitpos & 31U;
         const uint32_t w0 = __ldg(p), w1 = __ldg(p + 1);
+        pf = __ldg(p + 2);
+        src = p + 3;
         hi = __funnelshift_l(w1, w0, sh);
         lo = w1 << sh;
         avail = 64U - sh;
-        src = p + 2;
-        pf = __ldg(src);
     }
     // Drops n (< 32) bits; only the low five bits of n are used.
     __device__ __forceinline__ void consume(uint32_t n) {
@@ -73,25 +79,23 @@ struct Window {
         lo = __funnelshift_l(0U, lo, n);
         avail -= n & 31U;
     }
-    // Appends the prefetched word when at most 32 bits remain.
+    // Appends the next word when at most 32 bits remain.
     __device__ __forceinline__ void top_up() {
         if (avail <= 32U) {
             hi |= __funnelshift_rc(pf, 0U, avail);
             lo = __funnelshift_rc(0U, pf, avail);
             avail += 32U;
-            pf = __ldg(++src);
+            pf = __ldg(src++);
         }
     }
 };
 
 // Code longer than 12 bits: consume the 12-bit prefix, then walk the suffix
 // tree one bit at a time (at most 44 steps). Returns a leaf word (byte
-// count in bits 5..6, bytes in 8..23, zero shift). A table that exceeds the
+// count in bits 5..7, bytes in 8..23, zero shift). A table that exceeds the
 // depth sets *status and yields one zero byte, so the lane still finishes.
-__device__ __forceinline__ uint32_t walk_long(const uint32_t* __restrict__ table, uint32_t marker,
-                                            uint32_t& hi, uint32_t& lo, uint32_t& avail, uint32_t& pf,
-                                            const uint32_t*& src, int32_t* status) {
-    Window w{hi, lo, avail, pf, src};
+__device__ __forceinline__ uint32_t walk_long(const uint32_t* __restrict__ table, uint32_t marker, Window& w,
+                                              int32_t* status) {
     w.consume(NZ_LUT_BITS);
     uint32_t node = (marker >> 8) & kTreeMask;
     uint32_t leaf = 0;
@@ -99,8 +103,8 @@ __device__ __forceinline__ uint32_t walk_long(const uint32_t* __restrict__ table
         w.top_up();
         const uint32_t bit = w.hi >> 31;
         w.consume(1);
-        const uint32_t child = table[NZ_LUT_ENTRIES + 2U * node + bit];
-        if (child & 0x60U) {
+        const uint32_t child = table[NZ_LUT_TREE + 2U * node + bit];
+        if (child & 0xE0U) {
             leaf = child & ~0x1FU;
             break;
         }
@@ -110,11 +114,6 @@ __device__ __forceinline__ uint32_t walk_long(const uint32_t* __restrict__ table
         if (status) *status = kStatusCorruptTable;
         leaf = 1U << 5;
     }
-    hi = w.hi;
-    lo = w.lo;
-    avail = w.avail;
-    pf = w.pf;
-    src = w.src;
     return leaf;
 }
 
@@ -231,7 +230,7 @@ __global__ void __launch_bounds__(NW * 32, (NW >= 16 ? 2 : (NW >= 8 ? 4 : 8)))
                 const uint32_t e = tile_base + it * 256U + lane * 8U;
                 if (e >= numel) break;
                 if (sel_ok && e + 8U <= numel) {
-                    const uint2 x = ldg_u2(sel + e);
+                    const uint2 x = ldg_u2(sel + e);  // 8-byte aligned: sel_ok
                     uint2 r[L::kRawLanes];
 #pragma unroll
                     for (int l = 0; l < L::kRawLanes; ++l) r[l] = ldg_u2(lanes[l] + e);
@@ -264,7 +263,8 @@ __global__ void __launch_bounds__(NW * 32, (NW >= 16 ? 2 : (NW >= 8 ? 4 : 8)))
         Window win;
         win.init(reinterpret_cast<const uint32_t*>(g.bits),
                  reinterpret_cast<const uint32_t*>(g.tile_off)[item.tile] + incl - len);
-        // Byte queue qb:qa, `qbits` bits queued (< 32 between iterations).
+        // Byte queue qb:qa, `qbits` bits queued (<= 24 between iterations,
+        // <= 56 after a 4-byte push, so one flush per lookup suffices).
         uint32_t qa = 0, qb = 0, qbits = 0;
         uint32_t* row = stage + lane * kStageStride;
 
@@ -274,15 +274,17 @@ __global__ void __launch_bounds__(NW * 32, (NW >= 16 ? 2 : (NW >= 8 ? 4 : 8)))
             const uint32_t want = n_lane > done ? min(kRoundElems, n_lane - done) : 0U;
             const uint32_t target = (want + 3U) >> 2;
             for (uint32_t wi = 0; wi < target;) {
-                uint32_t e = table[win.hi >> (32 - NZ_LUT_BITS)];
-                if ((e & 0x60U) == 0U)
-                    e = walk_long(table, e, win.hi, win.lo, win.avail, win.pf, win.src, status);
+                const uint2 entry = reinterpret_cast<const uint2*>(table)[win.hi >> (32 - NZ_LUT_BITS)];
+                uint32_t e = entry.x, x = entry.y;
+                if ((e & 0xE0U) == 0U) {
+                    e = walk_long(table, e, win, status);
+                    x = e >> 8;
+                }
                 win.consume(e);
                 win.top_up();
-                const uint32_t x = e >> 8;
                 qa |= x << qbits;
                 qb |= __funnelshift_l(x, 0U, qbits);
-                qbits += (e >> 2) & 0x18U;
+                qbits += (e >> 2) & 0x38U;
                 if (qbits >= 32U) {
                     row[wi++] = qa;
                     qa = qb;

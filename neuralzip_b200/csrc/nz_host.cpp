@@ -117,17 +117,18 @@ std::vector<uint64_t> canonical_mixed_codes(const uint8_t* lengths, uint32_t nsy
     return codes;
 }
 
-// Multi-symbol decode table. Entry for a 12-bit window:
-//   bits  0..3   window bits the decoded tokens consume (1..12); bit 4 is
-//                zero so the low five bits are directly a shift amount
-//   bits  5..6   number of decoded bytes (1..3)
-//   bits  8..31  up to three decoded bytes (first byte lowest)
-// A window whose first code is longer than 12 bits holds instead the index
-// of the trie node reached after 12 bits (bits 8..31) with a zero byte
-// count; the kernel then walks the suffix tree stored after the 4096
-// entries, two words per node (child for bit 0, child for bit 1), where a
-// child with a nonzero byte count is a leaf (bytes in bits 8..23) and any
-// other child holds the next node index in bits 8..31.
+// Multi-symbol decode table: NZ_LUT_ENTRIES entries of two words, then the
+// suffix tree. Entry for a 12-bit window (word 0 / word 1):
+//   w0 bits 0..3  window bits the decoded tokens consume (1..12); bit 4 is
+//                 zero so the low five bits are directly a shift amount
+//   w0 bits 5..7  number of decoded bytes (1..4)
+//   w1            up to four decoded bytes (first byte lowest)
+// A window whose first code is longer than 12 bits instead has a zero byte
+// count and the index of the trie node reached after 12 bits in w0 bits
+// 8..31; the kernel then walks the suffix tree at word NZ_LUT_TREE, two
+// words per node (child for bit 0, child for bit 1): a child with a nonzero
+// byte count (bits 5..7) is a leaf with its bytes in bits 8..23, any other
+// child holds the next node index in bits 8..31.
 void Codebook::build_lut() {
     std::vector<TrieNode> trie(1);
     for (uint32_t s = 0; s < nsym; ++s) {
@@ -204,7 +205,7 @@ void Codebook::build_lut() {
     lut.assign(NZ_LUT_WORDS, 0);
     for (uint32_t prefix = 0; prefix < NZ_LUT_ENTRIES; ++prefix) {
         uint32_t pos = 0, nbytes = 0, bytes = 0;
-        uint32_t entry = 0;
+        uint32_t meta = 0;
         while (pos < NZ_LUT_BITS) {
             int node = 0;
             uint32_t depth = 0;
@@ -216,18 +217,19 @@ void Codebook::build_lut() {
                     throw Error(NZ_EVALUE, "The Huffman codebook does not cover every prefix.");
             }
             if (trie[node].symbol < 0) {
-                if (pos == 0) entry = static_cast<uint32_t>(trie[node].suffix) << 8;
+                if (pos == 0) meta = static_cast<uint32_t>(trie[node].suffix) << 8;
                 break;
             }
             uint32_t value = 0;
             const uint32_t count = token_bytes(trie[node].symbol, &value);
-            if (nbytes + count > 3) break;
+            if (nbytes + count > 4) break;
             bytes |= value << (8 * nbytes);
             nbytes += count;
             pos += depth;
         }
-        if (nbytes) entry = (bytes << 8) | pos | (nbytes << 5);
-        lut[prefix] = entry;
+        if (nbytes) meta = pos | (nbytes << 5);
+        lut[2 * prefix] = meta;
+        lut[2 * prefix + 1] = bytes;
     }
     // Suffix tree below depth 12.
     for (size_t i = 0; i < trie.size(); ++i) {
@@ -247,7 +249,7 @@ void Codebook::build_lut() {
             } else {
                 word = static_cast<uint32_t>(trie[child].suffix) << 8;
             }
-            lut[NZ_LUT_ENTRIES + 2 * static_cast<uint32_t>(node.suffix) + b] = word;
+            lut[NZ_LUT_TREE + 2 * static_cast<uint32_t>(node.suffix) + b] = word;
         }
     }
 }

@@ -151,10 +151,10 @@ static inline uint32_t decode_token(const Codebook& cb, uint64_t w, uint32_t* by
     }
     uint32_t node = e & (NZ_TREE_MAX_NODES - 1);
     for (uint32_t used = NZ_LUT_BITS; used < NZ_MAX_CODE_BITS; ++used) {
-        const uint32_t child = cb.lut[NZ_LUT_ENTRIES + 2 * node + ((w >> (63 - used)) & 1U)];
-        if (child & 0x60U) {
+        const uint32_t child = cb.lut[NZ_LUT_TREE + 2 * node + ((w >> (63 - used)) & 1U)];
+        if (child & 0xE0U) {
             *bytes = (child >> 8) & 0xFFFFU;
-            *count = (child >> 5) & 3U;
+            *count = (child >> 5) & 7U;
             return used + 1;
         }
         node = (child >> 8) & (NZ_TREE_MAX_NODES - 1);

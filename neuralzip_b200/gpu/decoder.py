@@ -29,7 +29,7 @@ import torch
 from neuralzip_b200 import _native
 
 KERNEL_PATH = Path(__file__).resolve().parent.parent / "csrc" / "nz_decode.cu"
-WARPS_PER_CTA = 8
+WARPS_PER_CTA = 16
 SM_COUNT_DEFAULT = 148
 
 
@@ -95,7 +95,7 @@ class TileDecoder:
         """(warps per CTA, works per CTA) for a launch of `total_works` tiles."""
         sms = self._sms(device_index)
         nw = WARPS_PER_CTA
-        resident = 4 * sms
+        resident = (64 // nw) * sms  # CTAs resident at 2048 threads per SM
         k = max(1, min(4, total_works // max(1, resident * nw)))
         return nw, nw * k
 
@@ -134,6 +134,9 @@ class TileDecoder:
         if any(g.spec != spec for g in groups):
             raise ValueError("A decode batch must use one layout.")
         table = np.zeros(len(groups), dtype=_native.GROUP_DTYPE)
+        for g in groups:
+            if g.lut_index != _native.RAW_LUT and (g.bits % 16 or g.lut_ptr % 16):
+                raise ValueError("Bitstreams and decode tables must be 16-byte aligned.")
         for i, g in enumerate(groups):
             table[i] = (g.bits, g.lens, g.tile_off, g.lanes, g.out, g.numel, g.lut_index)
         # Works sorted by decode table so each CTA stages one table.

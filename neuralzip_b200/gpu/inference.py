@@ -87,7 +87,7 @@ class GPUCodebook:
         """Words of the decode table the kernel stages (table + suffix tree)."""
         if self.native is None:
             return 0
-        return (_native.LUT_ENTRIES + 2 * self.native.tree_nodes + 3) // 4 * 4
+        return (_native.LUT_TREE + 2 * self.native.tree_nodes + 3) // 4 * 4
 
 
 @dataclass(frozen=True)

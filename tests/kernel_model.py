@@ -2,8 +2,8 @@
 
 Test helper: it runs the same per-lane algorithm as nz_tile_decode in
 neuralzip_b200/csrc/nz_decode.cu over the decode table produced by the
-product (nz_codebook_lut): 12-bit multi-byte table lookups whose low five
-bits are the shift amount, the suffix-tree walk for codes longer than 12
+product (nz_codebook_lut): 12-bit lookups of two-word entries (metadata
+whose low five bits are the shift amount, and up to four bytes), the suffix-tree walk for codes longer than 12
 bits, a byte queue flushed as 32-bit words, 128-element staging rounds, and
 only the staged prefix of the table (rounded up to 16 bytes) visible, so
 table, staging and loop errors show up on a CPU. Expected bytes always come
@@ -15,6 +15,7 @@ import numpy as np
 LANE, LANES, TILE = 256, 32, 8192
 ROUND = 128
 LUT_ENTRIES = 4096
+LUT_TREE = 2 * LUT_ENTRIES
 MASK64 = (1 << 64) - 1
 
 
@@ -67,25 +68,27 @@ def decode_group(lut, bits, lens, tile_off, numel, lut_words=None):
                 target = (want + 3) >> 2
                 staged = bytearray()
                 while len(staged) < 4 * target:
-                    e = int(table[win.buf >> 52])
-                    if (e & 0x60) == 0:
+                    k = win.buf >> 52
+                    e, x = int(table[2 * k]), int(table[2 * k + 1])
+                    if (e & 0xE0) == 0:
                         win.consume(12)
                         node = (e >> 8) & 511
                         for _ in range(44):
                             win.top_up()
                             bit = win.buf >> 63
                             win.consume(1)
-                            child = int(table[LUT_ENTRIES + 2 * node + bit])
-                            if child & 0x60:
+                            child = int(table[LUT_TREE + 2 * node + bit])
+                            if child & 0xE0:
                                 e = child & ~0x1F
+                                x = e >> 8
                                 break
                             node = (child >> 8) & 511
                         else:
                             raise AssertionError("suffix walk exceeded 44 steps")
                     win.consume(e)
                     win.top_up()
-                    queue |= (e >> 8) << qbits
-                    qbits += ((e >> 5) & 3) * 8
+                    queue |= x << qbits
+                    qbits += ((e >> 5) & 7) * 8
                     if qbits >= 32:
                         staged += (queue & 0xFFFFFFFF).to_bytes(4, "little")
                         queue >>= 32

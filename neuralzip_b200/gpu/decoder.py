@@ -95,8 +95,11 @@ class TileDecoder:
         """(warps per CTA, works per CTA) for a launch of `total_works` tiles."""
         sms = self._sms(device_index)
         nw = WARPS_PER_CTA
+        # Small launches: narrower CTAs so every SM gets at least two.
+        while nw > 4 and total_works < 2 * sms * nw:
+            nw //= 2
         resident = (64 // nw) * sms  # CTAs resident at 2048 threads per SM
-        k = max(1, min(4, total_works // max(1, resident * nw)))
+        k = max(1, min(2, total_works // max(1, resident * nw)))
         return nw, nw * k
 
     def _sms(self, device_index):

@@ -1,0 +1,188 @@
+"""C ABI, host codec and setup checks that need no GPU."""
+
+import ctypes
+import pickle
+import re
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+from torch import nn
+
+import helpers as H
+from neuralzip_b200 import _native, huff0
+from neuralzip_b200.compressor import NeuralZipCompressor
+from neuralzip_b200.dtypes import DTYPES
+from neuralzip_b200.gpu.inference import GPUCodebook, export_model_for_gpu
+from neuralzip_b200.setup import NeuralZipSetup
+from oracle import oracle as O
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "nz_b200.h"
+
+
+def test_library_exports_every_declared_symbol():
+    declared = set(re.findall(r"^int (nz_\w+)\(", HEADER.read_text(), flags=re.M))
+    assert declared == set(_native.EXPORTS)
+    lib = ctypes.CDLL(str(_native.library_path()))
+    for name in declared:
+        assert hasattr(lib, name), name
+    assert _native.load().nz_abi_version() == 1
+
+
+def test_struct_layouts_match_header(tmp_path):
+    """sizeof/offsetof of the C structs (compiled from the header) equal the
+    Python mirrors used to build device descriptors."""
+    import shutil
+    import subprocess
+
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    probe = tmp_path / "probe.c"
+    probe.write_text(
+        '#include <stdio.h>\n#include <stddef.h>\n#include "nz_b200.h"\n'
+        'int main(void){printf("%zu %zu %zu %zu %zu %zu %zu %zu\\n", sizeof(nz_group), sizeof(nz_work),'
+        ' sizeof(nz_cta), sizeof(nz_launch), sizeof(nz_pack_job), sizeof(nz_dtype),'
+        ' offsetof(nz_launch, n_ctas), offsetof(nz_group, numel)); return 0;}\n')
+    subprocess.run([cc, f"-I{HEADER.parent}", str(probe), "-o", str(tmp_path / "probe")], check=True)
+    sizes = [int(x) for x in subprocess.run([str(tmp_path / "probe")], capture_output=True, text=True,
+                                            check=True).stdout.split()]
+    assert sizes == [_native.GROUP_DTYPE.itemsize, _native.WORK_DTYPE.itemsize, _native.CTA_DTYPE.itemsize,
+                     ctypes.sizeof(_native.Launch), ctypes.sizeof(_native.PackJob), ctypes.sizeof(_native.Dtype),
+                     _native.Launch.n_ctas.offset, _native.GROUP_DTYPE.fields["numel"][1]]
+
+
+def test_error_mapping():
+    with pytest.raises(RuntimeError, match="Duplicate mixed pair"):
+        _native.export_code_table(b"NZM1" + bytes([9] * 258), 56, bytes((1, 2, 1, 2)))
+    with pytest.raises(RuntimeError, match="256 singletons"):
+        _native.export_code_table(b"NZM1" + bytes([8] * 100), 56)
+    with pytest.raises(ValueError, match="max_bits"):
+        _native.export_code_table(b"NZM1" + bytes([8] * 256), 0)
+    with pytest.raises(RuntimeError, match="Incomplete"):
+        _native.export_code_table(b"NZM1" + bytes([9] * 256), 56)
+    with pytest.raises(ValueError, match="code-length limit"):
+        GPUCodebook(tuple([13] + [8] * 255), tuple(range(256)))
+    with pytest.raises(ValueError, match="alphabet"):
+        GPUCodebook(tuple([8] * 257), tuple(range(257)))
+    with pytest.raises(ValueError):
+        _native.dtype_struct(3, 0, 7, 8, 1) and _native.split_lanes(b"\0" * 6, _native.dtype_struct(3, 0, 7, 8, 1))
+    with pytest.raises(RuntimeError, match="at least two"):
+        huff0.build_codebook_from_counts([5] + [0] * 255, prior_count=0, max_bits=12)
+    with pytest.raises(ValueError, match="256 entries"):
+        huff0.build_codebook_from_counts([1] * 10)
+
+
+@pytest.mark.parametrize("seed", range(8))
+def test_huff0_headers_round_trip(seed):
+    rng = np.random.default_rng(seed)
+    counts = np.zeros(256, dtype=np.uint64)
+    present = rng.choice(256, size=int(rng.integers(2, 257)), replace=False)
+    counts[present] = rng.geometric(0.02 if seed % 2 else 0.3, size=len(present))
+    book = huff0.build_codebook_from_counts(counts, prior_count=seed % 2, max_bits=12)
+    lengths, values, table_log, used = _native.huff0_read(book.codebook)
+    assert used == len(book.codebook) and table_log <= 12
+    lengths = np.frombuffer(lengths, dtype=np.uint8)
+    present_mask = (counts + (seed % 2)) > 0
+    assert np.array_equal(lengths > 0, present_mask)
+    kraft = sum(2.0 ** -int(length) for length in lengths if length)
+    assert kraft == 1.0
+    # Canonical values: longest codes first, symbol order within a length.
+    order = sorted((-int(length), s) for s, length in enumerate(lengths) if length)
+    codes = [(int(lengths[s]), values[s]) for _, s in order]
+    assert len(set(codes)) == len(codes)
+    # Huff0 4-stream blocks round trip through the product codec.
+    weights = (counts + (seed % 2)).astype(np.float64)
+    data = rng.choice(256, size=20000, p=weights / weights.sum()).astype(np.uint8)
+    block = _native.huff0_encode(book.handle, data, 2 * len(data))
+    assert block and np.array_equal(_native.huff0_decode(book.handle, block, len(data)), data)
+
+
+def test_uniform_alphabet_is_left_raw():
+    setup = NeuralZipSetup()
+    assert setup._singleton_codebook(np.full(256, 100, dtype=np.uint64)) is None
+
+
+class Model(nn.Module):
+    def __init__(self, dtype):
+        super().__init__()
+        self.layers = nn.ModuleList([nn.Linear(257, 513, bias=False, dtype=dtype),
+                                     nn.Linear(513, 17, bias=False, dtype=dtype)])
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+def test_storage_round_trip_and_export(dtype):
+    """The reference's CPU kernel check (_experiment_kernel_checks.py:134-174):
+    pattern weights, chunk_size 8192, bitwise storage round trip, packed
+    codebooks where the dtype has a pure exponent lane, and a raw fragment
+    between compressed chunks in the GPU export."""
+    model = Model(dtype)
+    with torch.no_grad():
+        for p in model.parameters():
+            p.copy_(H.pattern_weights(p.numel(), dtype).view_as(p))
+    named = dict(model.named_parameters())
+    setup = NeuralZipSetup(chunk_size=8192).build(named)
+    blob, metadata, sizes, seconds = NeuralZipCompressor(setup, threads=1).encode(named.items())
+    assert metadata["version"] == 2 and sizes["compressed_bytes"] < sizes["raw_bytes"]
+    decoded = NeuralZipCompressor().decode(blob, metadata)
+    assert all(torch.equal(decoded[n].view(torch.uint8), t.detach().view(torch.uint8)) for n, t in named.items())
+    key = next(iter(setup.chunk_codebooks))
+    ids = list(setup.chunk_codebooks[key])
+    ids[len(ids) // 2] = None
+    setup.chunk_codebooks[key] = tuple(ids)
+    exported = export_model_for_gpu(model, setup)
+    assert {b.tensor_name for b in exported.bindings} == set(named)
+    assert any(g.codebook_id == -1 for g in exported.groups)
+    if DTYPES[dtype].exponent_stream is not None:
+        assert any(g.codebook.vocab for g in exported.groups), "packed route not exercised"
+    # Every group decodes (CPU reader) to its slice of the original.
+    for g in exported.groups:
+        spec = g.encoded.dtype
+        sym = g.encoded.symbols
+        binding = g.bindings[0]
+        start = g.workspace_offset - binding.workspace_offset
+        raw = named[binding.tensor_name].detach().reshape(-1)[start:start + g.encoded.numel]
+        expected = H.selected_lane(raw.view(torch.uint8).numpy().tobytes(), spec)
+        if g.codebook.max_bits:
+            got = O.tile_decode(np.frombuffer(sym.bitstream, dtype=np.uint32), np.frombuffer(sym.lane_bits, np.uint16),
+                                np.asarray(sym.tile_offsets), g.encoded.numel, g.codebook.code_lengths,
+                                g.codebook.code_values, g.codebook.vocab)
+        else:
+            got = np.frombuffer(sym.bitstream, dtype=np.uint8)
+        assert np.array_equal(got, expected)
+
+
+def test_setup_pickle_and_options():
+    named = {"a.weight": (torch.randn(64, 4096) * 0.02).to(torch.bfloat16),
+             "b.weight": (torch.randn(64, 4096) * 1.0).to(torch.bfloat16)}
+    setup = NeuralZipSetup(chunk_size=64 << 10).build(named)
+    again = pickle.loads(pickle.dumps(setup))
+    assert again.chunk_codebooks == setup.chunk_codebooks and len(again.codebooks) == len(setup.codebooks)
+    assert NeuralZipSetup.load(again) is again
+    forced = NeuralZipSetup(chunk_size=64 << 10, cluster_map={"a.weight": 7, "b.weight": 7}).build(named)
+    ids = {i for v in forced.chunk_codebooks.values() for i in v}
+    assert len(ids) == 1  # one forced cluster for both tensors
+    off = NeuralZipSetup(enable_shared_codebooks=False, enable_packed_codebooks=False).build(named)
+    assert off.codebooks == () and all(i is None for v in off.chunk_codebooks.values() for i in v)
+    singleton_only = NeuralZipSetup(chunk_size=64 << 10, enable_packed_codebooks=False).build(named)
+    assert all(b.mode == "shared_huff0" for b in singleton_only.codebooks)
+    with pytest.raises(ValueError):
+        NeuralZipSetup(chunk_size=2)
+
+
+def test_multithreaded_pack_matches_single_chunk():
+    spec = DTYPES[torch.bfloat16]
+    raw = H.gaussian_raw(3 * 131072 + 5, 0.02, torch.bfloat16, 9)
+    sel = H.selected_lane(raw, spec)
+    lengths, vocab = H.mixed_book_for(sel)
+    book = GPUCodebook(tuple(lengths), tuple(int(c) for c in O.mixed_codes(lengths)), vocab)
+    from neuralzip_b200.gpu.inference import _pack_parallel, encode_with_codebook
+
+    parts = [raw[i:i + 2 * 131072] for i in range(0, len(raw), 2 * 131072)]
+    many = _pack_parallel([(np.frombuffer(p, dtype=np.uint8), book, spec) for p in parts], threads=4)
+    for part, enc in zip(parts, many):
+        one = encode_with_codebook(part, book, dtype=spec, stream_id=1)
+        assert bytes(enc.symbols.bitstream) == bytes(one.symbols.bitstream)
+        assert bytes(enc.symbols.lane_bits) == bytes(one.symbols.lane_bits)
+        assert enc.symbols.tile_offsets == one.symbols.tile_offsets

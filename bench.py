@@ -384,9 +384,11 @@ def main():
     traffic = None
     traffic_file = ROOT / "profiles" / "nz_tile_decode_bf16_traffic.txt"
     if traffic_file.is_file():
-        for line in traffic_file.read_text().splitlines():
-            if line.startswith("dram_bytes_per_elem"):
-                traffic = int(float(line.split("=")[1]) * main_batch.elements)
+        fields = dict(line.split("=", 1) for line in traffic_file.read_text().splitlines()
+                      if line.startswith(("dram_bytes_per_launch", "elements_per_launch")))
+        if len(fields) == 2:  # ncu capture of the full launch, scaled if the workload size differs
+            per_elem = float(fields["dram_bytes_per_launch "]) / float(fields["elements_per_launch "])
+            traffic = int(per_elem * main_batch.elements)
 
     cpu = None
     if rank == 0 and not args.no_cpu_baseline:

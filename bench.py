@@ -52,6 +52,10 @@ def parse_args():
     p.add_argument("--bf16-tensors", type=int, default=64, help="config 2 has 64")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--workload", choices=("config2", "config3", "config4"), default="config2",
+                   help="config2: bulk decode (default line); config3/4: batch-1 generation")
+    p.add_argument("--new-tokens", type=int, default=None)
+    p.add_argument("--no-overlap", action="store_true", help="sequential decode schedule")
     return p.parse_args()
 
 
@@ -272,9 +276,97 @@ def run_reference(args, world, rank):
     }))
 
 
+
+# ---- configs 3 and 4: batch-1 greedy generation -------------------------------------
+
+def _model_config(name):
+    from transformers import LlamaConfig, Qwen2Config
+
+    if name == "config3":  # Qwen2.5-0.5B architecture
+        return Qwen2Config(hidden_size=896, num_hidden_layers=24, num_attention_heads=14, num_key_value_heads=2,
+                           intermediate_size=4864, vocab_size=151936, tie_word_embeddings=True,
+                           max_position_embeddings=4096), 32, 128
+    return LlamaConfig(hidden_size=4096, num_hidden_layers=32, num_attention_heads=32, num_key_value_heads=8,
+                       intermediate_size=14336, vocab_size=128256, max_position_embeddings=4096), 128, 256
+
+
+def run_generation(args, world, rank, local):
+    """Random-init model of the config's architecture (N(0, 0.02), norms 1),
+    compressed through neuralzip.setup + the GPU export, then greedy
+    generation at batch 1; the uncompressed model generates the same tokens
+    first and its first-step logits must equal the compressed model's bit
+    for bit."""
+    from transformers import AutoModelForCausalLM
+
+    from neuralzip_b200.gpu.inference import NeuralZipRuntime, export_model_for_gpu
+    from neuralzip_b200.setup import NeuralZipSetup
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    config, prompt_len, new_tokens = _model_config(args.workload)
+    new_tokens = args.new_tokens or new_tokens
+    config._attn_implementation = "sdpa"
+    torch.manual_seed(0)
+    with torch.device(device):
+        model = AutoModelForCausalLM.from_config(config, dtype=torch.bfloat16).eval()
+    prompt = torch.randint(config.vocab_size, (1, prompt_len), generator=torch.Generator().manual_seed(1)).to(device)
+
+    def generate(m):
+        torch.cuda.synchronize(device)
+        t0 = time.perf_counter()
+        with torch.no_grad():
+            out = m.generate(prompt, max_new_tokens=new_tokens, min_new_tokens=new_tokens, do_sample=False,
+                             use_cache=True, pad_token_id=0)
+        torch.cuda.synchronize(device)
+        return out, time.perf_counter() - t0
+
+    with torch.no_grad():
+        ref_logits = model(prompt, use_cache=False).logits.float().cpu()
+    generate(model)  # warm-up
+    ref_tokens, ref_s = generate(model)
+    t0 = time.perf_counter()
+    setup = NeuralZipSetup().build(model)
+    exported = export_model_for_gpu(model, setup)
+    prep_s = time.perf_counter() - t0
+    runtime = NeuralZipRuntime.attach(model, exported, device=device, overlap=not args.no_overlap)
+    with torch.no_grad():
+        logits = model(prompt, use_cache=False).logits.float().cpu()
+    identical = bool(torch.equal(logits.view(torch.int32), ref_logits.view(torch.int32)))
+    generate(model)
+    tokens, comp_s = generate(model)
+    # Per-token decode work: one decode of every block.
+    decode_ms = []
+    stream = torch.cuda.current_stream(device)
+    for _ in range(3):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for name in exported.block_order:
+            runtime._decode_block(name)
+        b.record(stream)
+        torch.cuda.synchronize(device)
+        decode_ms.append(a.elapsed_time(b))
+    decoded = sum(g.encoded.numel * g.encoded.dtype.element_size for g in exported.groups)
+    if rank == 0:
+        print(json.dumps({
+            "metric": "batch-1 greedy generation tok/s, compressed weights decoded per layer per token",
+            "value": round(new_tokens / comp_s, 3), "unit": "tok/s", "n_gpus": 1, "higher_is_better": True,
+            "workload": args.workload, "uncompressed_tok_s": round(new_tokens / ref_s, 3),
+            "ratio_vs_uncompressed": round(ref_s / comp_s, 4), "tokens_identical": bool(torch.equal(tokens, ref_tokens)),
+            "first_step_logits_bitwise": identical, "overlap": runtime.overlap,
+            "decode_all_blocks_ms": round(min(decode_ms), 3),
+            "decode_gbs": round(decoded / (min(decode_ms) * 1e-3) / 1e9, 1),
+            "compressed_weights": len({b.tensor_name for b in exported.bindings}), "prep_s": round(prep_s, 1),
+            "config": {"workload": args.workload, "prompt": prompt_len, "new_tokens": new_tokens,
+                       "attn": "sdpa", "kv_cache": True},
+        }))
+
 def main():
     args = parse_args()
     world, rank, local = dist_setup()
+    if args.workload != "config2":
+        run_generation(args, world, rank, local)
+        barrier(world)
+        return
     if args.impl == "reference":
         run_reference(args, world, rank)
         barrier(world)
@@ -384,10 +476,10 @@ def main():
     traffic = None
     traffic_file = ROOT / "profiles" / "nz_tile_decode_bf16_traffic.txt"
     if traffic_file.is_file():
-        fields = dict(line.split("=", 1) for line in traffic_file.read_text().splitlines()
-                      if line.startswith(("dram_bytes_per_launch", "elements_per_launch")))
+        fields = {k.strip(): v.strip() for k, v in (line.split("=", 1) for line in traffic_file.read_text().splitlines()
+                                                    if line.startswith(("dram_bytes_per_launch", "elements_per_launch")))}
         if len(fields) == 2:  # ncu capture of the full launch, scaled if the workload size differs
-            per_elem = float(fields["dram_bytes_per_launch "]) / float(fields["elements_per_launch "])
+            per_elem = float(fields["dram_bytes_per_launch"]) / float(fields["elements_per_launch"])
             traffic = int(per_elem * main_batch.elements)
 
     cpu = None

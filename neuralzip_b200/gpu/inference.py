@@ -445,11 +445,6 @@ def _binding_module(model, binding):
     return module
 
 
-def _binding_view(workspaces, dtype, binding):
-    offset = binding.workspace_offset
-    return workspaces[dtype][offset:offset + binding.numel].view(binding.shape)
-
-
 def _group_arrays(group):
     """Host arrays of one group in upload order: name -> uint8 view."""
     encoded = group.encoded
@@ -480,18 +475,39 @@ class _UploadedGroup:
 
 
 class NeuralZipRuntime:
-    """Runtime attached to one model on one CUDA device."""
+    """Runtime attached to one model on one CUDA device.
 
-    def __init__(self, model, exported, device):
+    With ``overlap`` (the default when a model has two or more blocks) every
+    dtype gets two workspaces (ping-pong): block i decodes into buffer
+    i % 2, and while block i runs, block i + 1 is already being decoded on a
+    side stream. The two streams are ordered with CUDA events only: the
+    compute stream waits for "block i decoded" before block i runs, and the
+    side stream waits for "everything before block i enqueued" (which covers
+    block i - 1, the last reader of the buffer block i + 1 reuses) before it
+    decodes. A block reached out of order, and the direct ``_decode_block`` /
+    ``materialized_weights`` calls, first drain pending side decodes and then
+    decode on the current stream, as the reference does
+    (neuralzip/gpu/inference.py:476-509). ``workspaces[dtype]`` covers both
+    buffers."""
+
+    def __init__(self, model, exported, device, *, overlap=True):
         self.model = model
         self.export = exported
         self.device = torch.device(device)
         self._decoder = gpu_decoder.default_decoder()
         self._hook_handles = []
+        blocks = exported.block_order
+        self.overlap = bool(overlap) and len(blocks) > 1
+        buffers = 2 if self.overlap else 1
+        self._block_index = {name: i for i, name in enumerate(blocks)}
+        self._parity = {name: (i % 2 if self.overlap else 0) for i, name in enumerate(blocks)}
+        self._buffer_elems = dict(exported.workspace_sizes)
         self.workspaces = {
-            dtype: torch.empty(size, dtype=dtype, device=self.device)
+            dtype: torch.empty(size * buffers, dtype=dtype, device=self.device)
             for dtype, size in exported.workspace_sizes.items()
         }
+        self._side = torch.cuda.Stream(device=self.device) if self.overlap else None
+        self._pending = {}
         # Decode tables: one row of LUT_WORDS words per codebook id.
         book_ids = sorted({g.codebook_id for g in exported.groups if g.codebook.max_bits})
         self._lut_rows = {cid: row for row, cid in enumerate(book_ids)}
@@ -526,8 +542,8 @@ class NeuralZipRuntime:
             def addr(name, placed=placed):
                 return base + placed[name][0] if name in placed else 0
 
-            output = self.workspaces[spec.torch_dtype][group.workspace_offset:
-                                                       group.workspace_offset + group.encoded.numel]
+            start = group.workspace_offset + self._buffer_offset(group.block_name, spec.torch_dtype)
+            output = self.workspaces[spec.torch_dtype][start:start + group.encoded.numel]
             coded = bool(group.codebook.max_bits)
             row = self._lut_rows.get(group.codebook_id) if coded else None
             device_group = gpu_decoder.DeviceGroup(
@@ -555,7 +571,7 @@ class NeuralZipRuntime:
         torch.cuda.synchronize(self.device)
 
     @classmethod
-    def attach(cls, model, exported, *, device=None):
+    def attach(cls, model, exported, *, device=None, overlap=True):
         if hasattr(model, RUNTIME_ATTRIBUTE):
             raise RuntimeError("This model already has a NeuralZip runtime.")
         if not exported.groups:
@@ -576,25 +592,63 @@ class NeuralZipRuntime:
             module._parameters.pop("weight", None)
             module.__dict__.pop("weight", None)
         model.to(device).eval()
-        runtime = cls(model, exported, device)
+        runtime = cls(model, exported, device, overlap=overlap)
         runtime._install()
         return runtime
 
+    def _buffer_offset(self, block_name, dtype):
+        return self._parity[block_name] * self._buffer_elems[dtype]
+
+    def _binding_view(self, block_name, dtype, binding):
+        offset = binding.workspace_offset + self._buffer_offset(block_name, dtype)
+        return self.workspaces[dtype][offset:offset + binding.numel].view(binding.shape)
+
     def _install(self):
-        for items in self._groups_by_block.values():
+        for name, items in self._groups_by_block.items():
             for item in items:
                 for binding in item.group.bindings:
-                    _binding_module(self.model, binding).__dict__["weight"] = _binding_view(
-                        self.workspaces, item.group.encoded.dtype.torch_dtype, binding)
+                    _binding_module(self.model, binding).__dict__["weight"] = self._binding_view(
+                        name, item.group.encoded.dtype.torch_dtype, binding)
+        hook = self._pre_hook if self.overlap else self._decode_block
         for block_name in self.export.block_order:
             handle = _decode_hook_module(self.model, block_name).register_forward_pre_hook(
-                partial(self._decode_block, block_name), prepend=True)
+                partial(hook, block_name), prepend=True)
             self._hook_handles.append(handle)
         setattr(self.model, RUNTIME_ATTRIBUTE, self)
 
+    def _drain(self, stream):
+        """Makes `stream` wait for every pending side-stream decode."""
+        for event in self._pending.values():
+            stream.wait_event(event)
+        self._pending.clear()
+
     def _decode_block(self, block_name, _module=None, _args=None):
+        """Decodes one block on the current stream (reference semantics)."""
+        stream = torch.cuda.current_stream(self.device)
+        self._drain(stream)
         for prepared in self._prepared_batches[block_name]:
-            self._decoder.decode_batch(prepared)
+            self._decoder.decode_batch(prepared, stream)
+
+    def _pre_hook(self, block_name, _module=None, _args=None):
+        """Forward pre-hook of the overlapped schedule."""
+        compute = torch.cuda.current_stream(self.device)
+        event = self._pending.pop(block_name, None)
+        if event is None:
+            self._decode_block(block_name)
+        else:
+            compute.wait_event(event)
+        order = self.export.block_order
+        following = order[(self._block_index[block_name] + 1) % len(order)]
+        if self._parity[following] == self._parity[block_name] or following in self._pending:
+            return  # odd block count wrapping around: decoded when reached
+        free = torch.cuda.Event()
+        free.record(compute)  # covers the previous user of `following`'s buffer
+        self._side.wait_event(free)
+        for prepared in self._prepared_batches[following]:
+            self._decoder.decode_batch(prepared, self._side)
+        done = torch.cuda.Event()
+        done.record(self._side)
+        self._pending[following] = done
 
     def check_status(self):
         """Raises if any decode launch reported a corrupt table."""
@@ -614,5 +668,5 @@ class NeuralZipRuntime:
                     if binding.tensor_name in yielded:
                         continue
                     yielded.add(binding.tensor_name)
-                    weight = _binding_view(self.workspaces, item.group.encoded.dtype.torch_dtype, binding)
+                    weight = self._binding_view(block_name, item.group.encoded.dtype.torch_dtype, binding)
                     yield binding.tensor_name, weight.detach().to("cpu", copy=True)

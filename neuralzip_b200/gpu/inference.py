@@ -478,36 +478,52 @@ class NeuralZipRuntime:
     """Runtime attached to one model on one CUDA device.
 
     With ``overlap`` (the default when a model has two or more blocks) every
-    dtype gets two workspaces (ping-pong): block i decodes into buffer
-    i % 2, and while block i runs, block i + 1 is already being decoded on a
-    side stream. The two streams are ordered with CUDA events only: the
-    compute stream waits for "block i decoded" before block i runs, and the
-    side stream waits for "everything before block i enqueued" (which covers
-    block i - 1, the last reader of the buffer block i + 1 reuses) before it
-    decodes. A block reached out of order, and the direct ``_decode_block`` /
-    ``materialized_weights`` calls, first drain pending side decodes and then
-    decode on the current stream, as the reference does
-    (neuralzip/gpu/inference.py:476-509). ``workspaces[dtype]`` covers both
+    dtype gets ``prefetch_depth`` workspaces (2 = ping-pong): block i decodes
+    into buffer i % depth, and while block i runs, blocks i + 1 ..
+    i + depth - 1 are already being decoded on a side stream. The two streams
+    are ordered with CUDA events only: the compute stream waits for "block i
+    decoded" before block i runs, and the side stream waits for "everything
+    before block i enqueued" before it reuses a buffer, which covers the
+    buffer's previous reader (a prefetch whose buffer is still used by the
+    current or a later block is skipped and done when that block is
+    reached). A block reached out of order, and the direct ``_decode_block``
+    / ``materialized_weights`` calls, first drain pending side decodes and
+    then decode on the current stream, as the reference does
+    (neuralzip/gpu/inference.py:476-509). ``workspaces[dtype]`` covers all
     buffers."""
 
-    def __init__(self, model, exported, device, *, overlap=True):
+    def __init__(self, model, exported, device, *, overlap=True, prefetch_depth=2):
         self.model = model
         self.export = exported
         self.device = torch.device(device)
         self._decoder = gpu_decoder.default_decoder()
         self._hook_handles = []
         blocks = exported.block_order
-        self.overlap = bool(overlap) and len(blocks) > 1
-        buffers = 2 if self.overlap else 1
+        n = len(blocks)
+        self.overlap = bool(overlap) and n > 1
+        depth = max(2, int(prefetch_depth)) if self.overlap else 1
+        self.prefetch_depth = depth
         self._block_index = {name: i for i, name in enumerate(blocks)}
-        self._parity = {name: (i % 2 if self.overlap else 0) for i, name in enumerate(blocks)}
+        self._parity = {name: i % depth for i, name in enumerate(blocks)}
+        # The block that used the same buffer last before each block (cyclic).
+        self._prev_user = {}
+        for i, name in enumerate(blocks):
+            j = (i - 1) % n
+            while j % depth != i % depth and j != i:
+                j = (j - 1) % n
+            self._prev_user[name] = blocks[j]
         self._buffer_elems = dict(exported.workspace_sizes)
         self.workspaces = {
-            dtype: torch.empty(size * buffers, dtype=dtype, device=self.device)
+            dtype: torch.empty(size * depth, dtype=dtype, device=self.device)
             for dtype, size in exported.workspace_sizes.items()
         }
         self._side = torch.cuda.Stream(device=self.device) if self.overlap else None
         self._pending = {}
+        # Reused events per block: "buffer free" (compute) and "decoded" (side).
+        self._free_events = {name: torch.cuda.Event() for name in blocks} if self.overlap else {}
+        self._done_events = {name: torch.cuda.Event() for name in blocks} if self.overlap else {}
+        self._ahead = {name: tuple(blocks[(i + d) % n] for d in range(1, min(depth, n)))
+                       for i, name in enumerate(blocks)}
         # Decode tables: one row of LUT_WORDS words per codebook id.
         book_ids = sorted({g.codebook_id for g in exported.groups if g.codebook.max_bits})
         self._lut_rows = {cid: row for row, cid in enumerate(book_ids)}
@@ -571,7 +587,7 @@ class NeuralZipRuntime:
         torch.cuda.synchronize(self.device)
 
     @classmethod
-    def attach(cls, model, exported, *, device=None, overlap=True):
+    def attach(cls, model, exported, *, device=None, overlap=True, prefetch_depth=2):
         if hasattr(model, RUNTIME_ATTRIBUTE):
             raise RuntimeError("This model already has a NeuralZip runtime.")
         if not exported.groups:
@@ -592,7 +608,7 @@ class NeuralZipRuntime:
             module._parameters.pop("weight", None)
             module.__dict__.pop("weight", None)
         model.to(device).eval()
-        runtime = cls(model, exported, device, overlap=overlap)
+        runtime = cls(model, exported, device, overlap=overlap, prefetch_depth=prefetch_depth)
         runtime._install()
         return runtime
 
@@ -637,18 +653,27 @@ class NeuralZipRuntime:
             self._decode_block(block_name)
         else:
             compute.wait_event(event)
-        order = self.export.block_order
-        following = order[(self._block_index[block_name] + 1) % len(order)]
-        if self._parity[following] == self._parity[block_name] or following in self._pending:
-            return  # odd block count wrapping around: decoded when reached
-        free = torch.cuda.Event()
-        free.record(compute)  # covers the previous user of `following`'s buffer
-        self._side.wait_event(free)
-        for prepared in self._prepared_batches[following]:
-            self._decoder.decode_batch(prepared, self._side)
-        done = torch.cuda.Event()
-        done.record(self._side)
-        self._pending[following] = done
+        index = self._block_index
+        n = len(index)
+        here = index[block_name]
+        free = None
+        for following in self._ahead[block_name]:
+            if following in self._pending:
+                continue
+            # The buffer's previous reader must already be enqueued, i.e. lie
+            # before this block; a reader in [this block, following) has not run.
+            prev = index[self._prev_user[following]]
+            if (prev - here) % n < (index[following] - here) % n:
+                break
+            if free is None:
+                free = self._free_events[block_name]
+                free.record(compute)
+                self._side.wait_event(free)
+            for prepared in self._prepared_batches[following]:
+                self._decoder.decode_batch(prepared, self._side)
+            done = self._done_events[following]
+            done.record(self._side)
+            self._pending[following] = done
 
     def check_status(self):
         """Raises if any decode launch reported a corrupt table."""

@@ -1,4 +1,4 @@
-"""The overlapped decode schedule (side stream, ping-pong workspaces).
+"""The overlapped decode schedule (side stream, 2..4 rotating workspaces).
 
 Every case compares against the uncompressed model bit for bit and against
 the sequential schedule (the reference's: decode on the compute stream
@@ -43,8 +43,8 @@ def exact(a, b):
     return torch.equal(a.cpu().view(torch.uint8), b.cpu().view(torch.uint8))
 
 
-@pytest.mark.parametrize("n_layers", [2, 5, 6])
-def test_overlap_matches_uncompressed_and_sequential(n_layers):
+@pytest.mark.parametrize("n_layers,depth", [(2, 2), (5, 2), (6, 2), (2, 3), (5, 3), (7, 4), (3, 4)])
+def test_overlap_matches_uncompressed_and_sequential(n_layers, depth):
     model, setup = build(n_layers)
     x = torch.randn(4, model.layers[0][0].in_features, generator=torch.Generator().manual_seed(1)).to(torch.bfloat16)
     with torch.no_grad():
@@ -52,8 +52,9 @@ def test_overlap_matches_uncompressed_and_sequential(n_layers):
     sequential = copy.deepcopy(model)
     overlapped = copy.deepcopy(model)
     rt_seq = NeuralZipRuntime.attach(sequential, export_model_for_gpu(sequential, setup), device="cuda:0", overlap=False)
-    rt_ovl = NeuralZipRuntime.attach(overlapped, export_model_for_gpu(overlapped, setup), device="cuda:0")
-    assert rt_ovl.overlap and not rt_seq.overlap
+    rt_ovl = NeuralZipRuntime.attach(overlapped, export_model_for_gpu(overlapped, setup), device="cuda:0",
+                                     prefetch_depth=depth)
+    assert rt_ovl.overlap and not rt_seq.overlap and rt_ovl.prefetch_depth == depth
     for ws in list(rt_ovl.workspaces.values()) + list(rt_seq.workspaces.values()):
         ws.view(torch.uint8).fill_(0xA5)
     with torch.no_grad():
@@ -63,10 +64,11 @@ def test_overlap_matches_uncompressed_and_sequential(n_layers):
     rt_ovl.check_status()
 
 
-def test_out_of_order_blocks_and_materialize():
+@pytest.mark.parametrize("depth", [2, 3])
+def test_out_of_order_blocks_and_materialize(depth):
     model, setup = build(4)
     reference = copy.deepcopy(model).cuda()
-    runtime = NeuralZipRuntime.attach(model, export_model_for_gpu(model, setup), device="cuda:0")
+    runtime = NeuralZipRuntime.attach(model, export_model_for_gpu(model, setup), device="cuda:0", prefetch_depth=depth)
     x = torch.randn(2, model.layers[0][0].in_features).to(torch.bfloat16).cuda()
     with torch.no_grad():
         model(x)  # leaves a prefetch of block 0 pending for the next forward

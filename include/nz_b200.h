@@ -20,8 +20,8 @@
  * length of sub-stream s and `tile_off[t]` the bit offset of tile t's first
  * sub-stream; a lane finds its start with a warp scan of its tile's lens.
  * A pair token never straddles two sub-streams. The bitstream starts on a
- * 16-byte boundary and ends with at least NZ_BITS_PAD_WORDS zero words (the
- * kernel reads ahead in 16-byte blocks). The non-selected byte lanes are
+ * 16-byte boundary and ends with at least NZ_BITS_PAD_WORDS zero words (a
+ * lane reads up to three words past its sub-stream). The non-selected byte lanes are
  * stored raw, one byte per element, 16-byte aligned.
  */
 #ifndef NZ_B200_H
@@ -223,7 +223,7 @@ typedef struct nz_cta {
  * pointers to NZ_LUT_WORDS-word tables. `status` (device int32) receives a
  * nonzero code if a corrupt table made a lane give up; it is only written
  * on error. Asynchronous on `cuda_stream` (a cudaStream_t, NULL = legacy
- * default stream). warps_per_cta: 1..32 (0 = default). */
+ * default stream). warps_per_cta: 4, 8 or 16 (0 = default, 8). */
 typedef struct nz_launch {
     nz_dtype dtype;
     uint32_t warps_per_cta;

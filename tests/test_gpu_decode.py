@@ -228,3 +228,32 @@ def test_launch_rejects_bad_geometry():
     launch.groups = launch.works = launch.ctas = launch.luts = 1
     with pytest.raises(ValueError):
         _native.decode_launch(launch, 0)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+def test_tiny_and_ragged_groups(dtype):
+    """Groups of 1, 7, 9, 255, 257 and 8193 elements in one launch (partial
+    sub-streams, partial tiles, scalar tails), singleton and mixed books."""
+    spec = DTYPES[dtype]
+    decoder = gpu_decoder.default_decoder()
+    arena, groups, expected = [], [], []
+    for i, numel in enumerate((1, 7, 9, 255, 257, 8193)):
+        raw = H.gaussian_raw(numel, [0.02, 1.0][i % 2], dtype, 40 + i)
+        sel = H.selected_lane(raw, spec)
+        if spec.exponent_stream is not None and i % 2:
+            lengths, vocab = H.mixed_book_for(sel)
+            book = GPUCodebook(tuple(lengths), tuple(int(v) for v in O.mixed_codes(lengths)), vocab)
+        else:
+            header, _ = _native.huff0_build(np.bincount(sel, minlength=256) * 64 + 1, 12)
+            lengths, values, _, _ = _native.huff0_read(header)
+            book = GPUCodebook(tuple(lengths), values)
+        out = torch.full((numel,), -1, dtype=torch.int16 if spec.element_size == 2 else torch.int32,
+                         device="cuda").view(dtype)
+        groups.append(_device_group(raw, spec, book, out, arena))
+        expected.append(raw)
+    prepared = decoder.prepare_batch(groups)
+    decoder.decode_batch(prepared)
+    torch.cuda.synchronize()
+    for g, raw in zip(groups, expected):
+        assert bytes(g.output.cpu().view(torch.uint8).numpy()) == raw
+    decoder.check_status(prepared)

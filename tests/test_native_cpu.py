@@ -99,6 +99,22 @@ def test_huff0_headers_round_trip(seed):
     assert block and np.array_equal(_native.huff0_decode(book.handle, block, len(data)), data)
 
 
+def test_empty_batch_and_zero_cta_launch():
+    """An empty batch is refused on the host; a launch with no CTAs is a
+    no-op that touches no device state (so it runs without a GPU)."""
+    from neuralzip_b200.gpu import decoder as gpu_decoder
+
+    with pytest.raises(ValueError, match="at least one group"):
+        gpu_decoder.default_decoder().prepare_batch([])
+    launch = _native.Launch()
+    launch.dtype = _native.dtype_struct(2, 1, 7, 8, 1)
+    launch.n_ctas = 0
+    _native.decode_launch(launch, 0)
+    launch.n_ctas = 1
+    with pytest.raises(ValueError, match="Null device"):
+        _native.decode_launch(launch, 0)
+
+
 def test_uniform_alphabet_is_left_raw():
     setup = NeuralZipSetup()
     assert setup._singleton_codebook(np.full(256, 100, dtype=np.uint64)) is None

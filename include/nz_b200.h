@@ -237,6 +237,11 @@ typedef struct nz_launch {
 } nz_launch;
 int nz_decode_launch(const nz_launch* launch, void* cuda_stream);
 
+/* Resident CTAs per SM of the decode kernel for `dtype` at warps_per_cta
+ * (the CUDA occupancy calculator on the current device; no reference
+ * counterpart: the reference sizes its grid per group, decoder.py:89-119). */
+int nz_decode_occupancy(const nz_dtype* dtype, uint32_t warps_per_cta,
+                        uint32_t* ctas_per_sm);
 /* Dynamic shared memory one CTA of nz_decode_launch uses. */
 int nz_decode_smem_bytes(uint32_t warps_per_cta, uint32_t* bytes);
 

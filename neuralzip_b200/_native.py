@@ -74,7 +74,8 @@ EXPORTS = (
     "nz_export_code_table", "nz_codebook_create", "nz_codebook_destroy", "nz_codebook_info",
     "nz_codebook_lut", "nz_huff0_build", "nz_huff0_read", "nz_pack_bound", "nz_pack_chunk",
     "nz_pack_many", "nz_split_lanes", "nz_exponent_histograms", "nz_count_tokens", "nz_mixed_encode", "nz_mixed_decode",
-    "nz_huff0_encode", "nz_huff0_decode", "nz_decode_launch", "nz_decode_smem_bytes", "nz_last_error",
+    "nz_huff0_encode", "nz_huff0_decode", "nz_decode_launch", "nz_decode_occupancy", "nz_decode_smem_bytes",
+    "nz_last_error",
     "nz_abi_version",
 )
 
@@ -128,6 +129,7 @@ def _declare(lib):
         "nz_huff0_encode": [c.c_void_p, c.c_void_p, c.c_uint64, c.c_void_p, c.c_uint64, u64p],
         "nz_huff0_decode": [c.c_void_p, c.c_void_p, c.c_uint64, c.c_void_p, c.c_uint64],
         "nz_decode_launch": [c.POINTER(Launch), c.c_void_p],
+        "nz_decode_occupancy": [c.POINTER(Dtype), c.c_uint32, u32p],
         "nz_decode_smem_bytes": [c.c_uint32, u32p],
         "nz_last_error": [c.c_char_p, c.c_size_t],
         "nz_abi_version": [],
@@ -359,6 +361,14 @@ def decode_smem_bytes(warps_per_cta=8):
     lib = load()
     out = ctypes.c_uint32()
     check(lib.nz_decode_smem_bytes(int(warps_per_cta), ctypes.byref(out)))
+    return out.value
+
+
+def decode_occupancy(dt, warps_per_cta):
+    """Resident decode CTAs per SM on the current CUDA device."""
+    lib = load()
+    out = ctypes.c_uint32()
+    check(lib.nz_decode_occupancy(ctypes.byref(dt), int(warps_per_cta), ctypes.byref(out)))
     return out.value
 
 

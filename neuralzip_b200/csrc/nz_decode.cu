@@ -50,6 +50,14 @@ __device__ __forceinline__ uint2 ldg_u2(const void* p) {
     return v;
 }
 
+// Asks L2 to fetch [p, p + bytes) ahead of use; p is 16-byte aligned and
+// bytes is rounded down to a multiple of 16 (a hint: nothing is written).
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+    bytes &= ~15U;
+    if (bytes)
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 __device__ __forceinline__ void stg_u4(void* p, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
     *reinterpret_cast<uint4*>(p) = make_uint4(a, b, c, d);
 }
@@ -260,6 +268,22 @@ __global__ void __launch_bounds__(NW * 32, (NW >= 16 ? 2 : (NW >= 8 ? 4 : 8)))
             const uint32_t v = __shfl_up_sync(0xFFFFFFFFU, incl, d);
             if (lane >= d) incl += v;
         }
+        // The tile's bits and raw lanes go to L2 now: the refills and the
+        // merges then wait for L2, not DRAM. The bit range is widened to
+        // 16-byte bounds, which stay inside the stream and its zero pad; a
+        // raw lane's ragged end (< 16 bytes) is left to the loads.
+        const uint32_t tile_bits = __shfl_sync(0xFFFFFFFFU, incl, 31);
+        if (lane == 0) {
+            const uint32_t b0 = reinterpret_cast<const uint32_t*>(g.tile_off)[item.tile];
+            const uint32_t w0 = (b0 >> 5) & ~3U;
+            const uint32_t w1 = ((b0 + tile_bits + 127U) >> 7) << 2;
+            prefetch_l2(reinterpret_cast<const uint32_t*>(g.bits) + w0, (w1 - w0) * 4U);
+            if (vec_ok) {
+                const uint32_t n = min(NZ_TILE_ELEMS, numel - tile_base);
+#pragma unroll
+                for (int l = 0; l < L::kRawLanes; ++l) prefetch_l2(lanes[l] + tile_base, n);
+            }
+        }
         Window win;
         win.init(reinterpret_cast<const uint32_t*>(g.bits),
                  reinterpret_cast<const uint32_t*>(g.tile_off)[item.tile] + incl - len);
@@ -327,17 +351,28 @@ __global__ void __launch_bounds__(NW * 32, (NW >= 16 ? 2 : (NW >= 8 ? 4 : 8)))
 }
 
 template <int ES, bool REORDER, int NW>
-cudaError_t launch_one(const nz_launch& l, cudaStream_t stream) {
+constexpr size_t smem_bytes() {
+    return (NZ_LUT_WORDS + NW * kStageWordsPerWarp) * sizeof(uint32_t);
+}
+
+// Opts the instantiation into its dynamic shared memory (once per process).
+template <int ES, bool REORDER, int NW>
+cudaError_t ensure_smem_attribute() {
     static std::once_flag once;
-    static cudaError_t attr_err = cudaSuccess;
-    const size_t smem = (NZ_LUT_WORDS + NW * kStageWordsPerWarp) * sizeof(uint32_t);
+    static cudaError_t err = cudaSuccess;
     std::call_once(once, [&]() {
-        attr_err = cudaFuncSetAttribute(nz_tile_decode<ES, REORDER, NW>,
-                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        static_cast<int>(smem));
+        err = cudaFuncSetAttribute(nz_tile_decode<ES, REORDER, NW>,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   static_cast<int>(smem_bytes<ES, REORDER, NW>()));
     });
+    return err;
+}
+
+template <int ES, bool REORDER, int NW>
+cudaError_t launch_one(const nz_launch& l, cudaStream_t stream) {
+    const cudaError_t attr_err = ensure_smem_attribute<ES, REORDER, NW>();
     if (attr_err != cudaSuccess) return attr_err;
-    nz_tile_decode<ES, REORDER, NW><<<l.n_ctas, NW * 32, smem, stream>>>(
+    nz_tile_decode<ES, REORDER, NW><<<l.n_ctas, NW * 32, smem_bytes<ES, REORDER, NW>(), stream>>>(
         reinterpret_cast<const nz_group*>(l.groups), reinterpret_cast<const nz_work*>(l.works),
         reinterpret_cast<const nz_cta*>(l.ctas), reinterpret_cast<const uint64_t*>(l.luts),
         reinterpret_cast<int32_t*>(l.status));
@@ -353,6 +388,35 @@ cudaError_t launch_nw(const nz_launch& l, cudaStream_t stream) {
     }
 }
 
+template <int ES, bool REORDER, int NW>
+cudaError_t occupancy_one(int* ctas) {
+    const cudaError_t err = ensure_smem_attribute<ES, REORDER, NW>();
+    if (err != cudaSuccess) return err;
+    return cudaOccupancyMaxActiveBlocksPerMultiprocessor(ctas, nz_tile_decode<ES, REORDER, NW>, NW * 32,
+                                                         smem_bytes<ES, REORDER, NW>());
+}
+
+template <int ES, bool REORDER>
+cudaError_t occupancy_nw(uint32_t nw, int* ctas) {
+    switch (nw) {
+        case 4: return occupancy_one<ES, REORDER, 4>(ctas);
+        case 16: return occupancy_one<ES, REORDER, 16>(ctas);
+        default: return occupancy_one<ES, REORDER, 8>(ctas);
+    }
+}
+
+enum class Kind { kBf16, kFp16, kFp32, kNone };
+
+Kind kind_of(const nz_dtype& d) {
+    if (d.elem_size == 2 && d.stream_id == 1 && d.reorder && d.mant_bits == 7 && d.exp_bits == 8)
+        return Kind::kBf16;
+    if (d.elem_size == 2 && d.stream_id == 1 && !d.reorder && d.mant_bits == 10 && d.exp_bits == 5)
+        return Kind::kFp16;
+    if (d.elem_size == 4 && d.stream_id == 3 && d.reorder && d.mant_bits == 23 && d.exp_bits == 8)
+        return Kind::kFp32;
+    return Kind::kNone;
+}
+
 }  // namespace
 
 extern "C" {
@@ -361,6 +425,25 @@ int nz_decode_smem_bytes(uint32_t warps_per_cta, uint32_t* bytes) {
     if (!bytes) return nz::fail(NZ_EVALUE, "Null output.");
     const uint32_t nw = warps_per_cta == 0 ? 8U : warps_per_cta;
     *bytes = (NZ_LUT_WORDS + nw * kStageWordsPerWarp) * static_cast<uint32_t>(sizeof(uint32_t));
+    return NZ_OK;
+}
+
+int nz_decode_occupancy(const nz_dtype* dtype, uint32_t warps_per_cta, uint32_t* ctas_per_sm) {
+    if (!dtype || !ctas_per_sm) return nz::fail(NZ_EVALUE, "Null argument.");
+    if (warps_per_cta != 0 && warps_per_cta != 4 && warps_per_cta != 8 && warps_per_cta != 16)
+        return nz::fail(NZ_EVALUE, "warps_per_cta must be 4, 8 or 16.");
+    int ctas = 0;
+    cudaError_t err;
+    switch (kind_of(*dtype)) {
+        case Kind::kBf16: err = occupancy_nw<2, true>(warps_per_cta, &ctas); break;
+        case Kind::kFp16: err = occupancy_nw<2, false>(warps_per_cta, &ctas); break;
+        case Kind::kFp32: err = occupancy_nw<4, true>(warps_per_cta, &ctas); break;
+        default:
+            return nz::fail(NZ_EVALUE, "Unsupported GPU layout (bf16, fp16 and fp32 are decoded).");
+    }
+    if (err != cudaSuccess)
+        return nz::fail(NZ_ECUDA, std::string("CUDA occupancy query failed: ") + cudaGetErrorString(err));
+    *ctas_per_sm = static_cast<uint32_t>(ctas);
     return NZ_OK;
 }
 
@@ -373,19 +456,15 @@ int nz_decode_launch(const nz_launch* launch, void* cuda_stream) {
     if (l.warps_per_cta != 0 && l.warps_per_cta != 4 && l.warps_per_cta != 8 &&
         l.warps_per_cta != 16)
         return nz::fail(NZ_EVALUE, "warps_per_cta must be 4, 8 or 16.");
-    const nz_dtype& d = l.dtype;
     cudaStream_t stream = reinterpret_cast<cudaStream_t>(cuda_stream);
     cudaError_t err;
-    if (d.elem_size == 2 && d.stream_id == 1 && d.reorder && d.mant_bits == 7 && d.exp_bits == 8)
-        err = launch_nw<2, true>(l, stream);
-    else if (d.elem_size == 2 && d.stream_id == 1 && !d.reorder && d.mant_bits == 10 &&
-             d.exp_bits == 5)
-        err = launch_nw<2, false>(l, stream);
-    else if (d.elem_size == 4 && d.stream_id == 3 && d.reorder && d.mant_bits == 23 &&
-             d.exp_bits == 8)
-        err = launch_nw<4, true>(l, stream);
-    else
-        return nz::fail(NZ_EVALUE, "Unsupported GPU layout (bf16, fp16 and fp32 are decoded).");
+    switch (kind_of(l.dtype)) {
+        case Kind::kBf16: err = launch_nw<2, true>(l, stream); break;
+        case Kind::kFp16: err = launch_nw<2, false>(l, stream); break;
+        case Kind::kFp32: err = launch_nw<4, true>(l, stream); break;
+        default:
+            return nz::fail(NZ_EVALUE, "Unsupported GPU layout (bf16, fp16 and fp32 are decoded).");
+    }
     if (err != cudaSuccess)
         return nz::fail(NZ_ECUDA, std::string("CUDA launch failed: ") + cudaGetErrorString(err));
     return NZ_OK;

@@ -13,8 +13,9 @@ kernel is prebuilt in libnzb200.so and reached through the C ABI
 whatever its codebook (singleton, mixed, long codes, raw), so a block needs
 one launch per dtype instead of one per (layout, staging) combination. The
 launch geometry is a list of (group, tile) works cut into CTAs that share a
-decode table; ``staging_policy`` (warps per CTA, works per CTA) can be
-overridden the way the reference's tests override ``_staging``.
+decode table; ``staging_policy`` (warps per CTA, works per CTA of each
+table) can be overridden the way the reference's tests override
+``_staging``.
 """
 
 from __future__ import annotations
@@ -31,6 +32,8 @@ from neuralzip_b200 import _native
 KERNEL_PATH = Path(__file__).resolve().parent.parent / "csrc" / "nz_decode.cu"
 WARPS_PER_CTA = 16
 SM_COUNT_DEFAULT = 148
+# A raw tile (no Huffman decode) takes about a quarter of a coded tile's time.
+RAW_WORK_WEIGHT = 4
 
 
 def shared_memory_bytes(warps_per_cta=WARPS_PER_CTA, max_elements=None):
@@ -89,18 +92,50 @@ class TileDecoder:
 
     def __init__(self):
         self._sm_count = {}
+        self._ctas_per_sm = {}
 
     # Reference hook: the staging policy decides the launch geometry.
-    def staging_policy(self, device_index, total_works):
-        """(warps per CTA, works per CTA) for a launch of `total_works` tiles."""
+    def staging_policy(self, device_index, lut_works, layout=None):
+        """Launch geometry for a batch with ``lut_works[lut] = (works, raw)``
+        tiles per decode table: (warps per CTA, {lut: works per CTA}).
+
+        Every CTA stages one table and its warps take the CTA's works in
+        turn, so they get equal counts (+-1). The works per warp are the
+        smallest count whose CTAs fit in one wave of resident CTAs: a launch
+        then ends when its busiest warps do, instead of with a partial last
+        wave that leaves SMs idle. Small launches use narrower CTAs so that
+        every SM gets work."""
         sms = self._sms(device_index)
+        total = sum(n for n, _ in lut_works.values())
         nw = WARPS_PER_CTA
-        # Small launches: narrower CTAs so every SM gets at least two.
-        while nw > 4 and total_works < 2 * sms * nw:
+        while nw > 4 and total < 2 * sms * nw:
             nw //= 2
-        resident = (64 // nw) * sms  # CTAs resident at 2048 threads per SM
-        k = max(1, min(2, total_works // max(1, resident * nw)))
-        return nw, nw * k
+        slots = self._occupancy(device_index, layout, nw) * sms
+
+        def weight(raw):
+            return RAW_WORK_WEIGHT if raw else 1
+
+        def ctas(per_warp):
+            return sum(-(-n // (nw * per_warp * weight(raw))) for n, raw in lut_works.values())
+
+        per_warp = max(1, -(-total // (slots * nw)))
+        while ctas(per_warp) > slots:
+            per_warp += 1
+        return nw, {lut: nw * per_warp * weight(raw) for lut, (_, raw) in lut_works.items()}
+
+    def _occupancy(self, device_index, layout, nw):
+        """Resident CTAs per SM (CUDA occupancy calculator; shared memory
+        allows 2, 3 and 4 CTAs of 16, 8 and 4 warps on a B200)."""
+        key = (device_index, layout, nw)
+        if key not in self._ctas_per_sm:
+            fallback = {16: 2, 8: 3, 4: 4}[nw]
+            try:
+                with torch.cuda.device(device_index):
+                    dt = _native.dtype_struct(*layout) if layout else _native.dtype_struct(2, True, 7, 8, 1)
+                    self._ctas_per_sm[key] = _native.decode_occupancy(dt, nw) or fallback
+            except (RuntimeError, AssertionError, TypeError):
+                self._ctas_per_sm[key] = fallback
+        return self._ctas_per_sm[key]
 
     def _sms(self, device_index):
         if device_index not in self._sm_count:
@@ -152,7 +187,11 @@ class TileDecoder:
             table[i]["lut"] = _native.RAW_LUT if g.lut_index == _native.RAW_LUT else lut_slot[g.lut_index]
         order = sorted(range(len(groups)), key=lambda i: (groups[i].lut_index, i))
         total_works = sum(groups[i].tiles for i in order)
-        nw, per_cta = self.staging_policy(device.index, total_works)
+        lut_works = {lut: (sum(g.tiles for g in groups if g.lut_index == lut), lut == _native.RAW_LUT)
+                     for lut in lut_ids}
+        layout = (spec.element_size, bool(spec.bit_reorder), spec.mantissa_bits, spec.exponent_bits,
+                  spec.gpu_stream)
+        nw, per_cta = self.staging_policy(device.index, lut_works, layout)
         works = np.zeros(total_works, dtype=_native.WORK_DTYPE)
         ctas = []
         cursor = 0
@@ -167,8 +206,9 @@ class TileDecoder:
                 cursor += n
             slot = _native.RAW_LUT if lut == _native.RAW_LUT else lut_slot[lut]
             words = 0 if lut == _native.RAW_LUT else lut_words[lut]
-            for start in range(begin, cursor, per_cta):
-                ctas.append((slot, start, min(cursor, start + per_cta), words))
+            step = max(1, int(per_cta[lut]))
+            for start in range(begin, cursor, step):
+                ctas.append((slot, start, min(cursor, start + step), words))
         cta_array = np.array(ctas, dtype=_native.CTA_DTYPE)
         if not len(lut_ptrs):
             lut_ptrs = np.zeros(1, dtype=np.uint64)
@@ -183,8 +223,6 @@ class TileDecoder:
         launch.groups, launch.works, launch.ctas, launch.luts = (t.data_ptr() for t in tensors)
         launch.status = status.data_ptr()
         launch.n_ctas = len(cta_array)
-        layout = (spec.element_size, bool(spec.bit_reorder), spec.mantissa_bits, spec.exponent_bits,
-                  spec.gpu_stream)
         return PreparedBatch(
             descriptor_tensors=tensors, device=device, layout=layout, warps_per_cta=nw,
             shared_memory=shared_memory_bytes(nw), kernel_grid=(len(cta_array),), launch=launch,

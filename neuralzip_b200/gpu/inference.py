@@ -351,7 +351,7 @@ def _pack_parallel(items, threads=0):
         for job, (index, _raw, bits, lens, tile_off, lanes, numel, book) in zip(done, keep):
             streams = [_view(lane) if lane is not None else None for lane in lanes]
             streams[spec.gpu_stream] = GPUEncodedSymbols(
-                _view(bits[:job.words_used]), int(job.bit_length), numel, _view(lens),
+                _view(bits[:job.words_used].copy()), int(job.bit_length), numel, _view(lens),
                 tuple(tile_off.tolist()))
             results[index] = GPUEncoded(spec, numel, tuple(streams))
     return results

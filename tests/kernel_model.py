@@ -23,12 +23,15 @@ class _Window:
     """hi:lo as one 64-bit integer; valid bits are the top `avail` bits."""
 
     def __init__(self, words, bitpos):
+        # Same loads as the kernel: two words into the window and the next
+        # one requested ahead, so an out-of-range read raises IndexError here.
         self.words = words
         p = bitpos >> 5
         sh = bitpos & 31
         self.buf = (((int(words[p]) << 32) | int(words[p + 1])) << sh) & MASK64
         self.avail = 64 - sh
-        self.ptr = p + 2
+        self.pf = int(words[p + 2])
+        self.ptr = p + 3
 
     def consume(self, n):
         n &= 31
@@ -37,8 +40,9 @@ class _Window:
 
     def top_up(self):
         if self.avail <= 32:
-            self.buf |= (int(self.words[self.ptr]) << 32) >> self.avail
+            self.buf |= (self.pf << 32) >> self.avail
             self.avail += 32
+            self.pf = int(self.words[self.ptr])
             self.ptr += 1
 
 

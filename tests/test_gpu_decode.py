@@ -140,8 +140,9 @@ def test_multi_codebook_batch_with_raw_fragment(dtype):
     runtime.check_status()
 
 
-def _device_group(raw, spec, book, out_tensor, arena):
-    """Uploads one group by hand; returns its DeviceGroup."""
+def _device_group(raw, spec, book, out_tensor, arena, lut_index=0):
+    """Uploads one group by hand; returns its DeviceGroup. Groups of one
+    batch that use different tables need different `lut_index` values."""
     enc = encode_with_codebook(raw, book, dtype=spec, stream_id=spec.gpu_stream)
     sym = enc.symbols
     pieces = {"bits": sym.bitstream, "lens": sym.lane_bits,
@@ -157,7 +158,7 @@ def _device_group(raw, spec, book, out_tensor, arena):
     lut = torch.from_numpy(np.asarray(book.decode_lut, dtype=np.uint32).view(np.int32)).to("cuda")
     arena.append(lut)
     return gpu_decoder.DeviceGroup(
-        spec=spec, numel=enc.numel, lut_index=id(book) & 0xFFFF, lut_ptr=lut.data_ptr(),
+        spec=spec, numel=enc.numel, lut_index=lut_index, lut_ptr=lut.data_ptr(),
         lut_words=book.table_words, bits=addr["bits"], lens=addr["lens"], tile_off=addr["tile_off"],
         lanes=tuple(addr.get(f"lane{lane}", 0) for lane in range(4)), out=out_tensor.data_ptr(),
         output=out_tensor)
@@ -249,7 +250,7 @@ def test_tiny_and_ragged_groups(dtype):
             book = GPUCodebook(tuple(lengths), values)
         out = torch.full((numel,), -1, dtype=torch.int16 if spec.element_size == 2 else torch.int32,
                          device="cuda").view(dtype)
-        groups.append(_device_group(raw, spec, book, out, arena))
+        groups.append(_device_group(raw, spec, book, out, arena, lut_index=i))
         expected.append(raw)
     prepared = decoder.prepare_batch(groups)
     decoder.decode_batch(prepared)

@@ -57,6 +57,10 @@ def parse_args():
     p.add_argument("--new-tokens", type=int, default=None)
     p.add_argument("--no-overlap", action="store_true", help="sequential decode schedule")
     p.add_argument("--prefetch-depth", type=int, default=2, help="decode buffers per dtype in the overlapped schedule")
+    p.add_argument("--blocks-per-launch", type=int, default=0,
+                   help="consecutive blocks decoded by one launch (0 = auto)")
+    p.add_argument("--batch", type=int, default=1, help="generation batch (config 4 also names 8)")
+    p.add_argument("--gen-reps", type=int, default=3, help="alternating timed runs per model")
     return p.parse_args()
 
 
@@ -294,9 +298,13 @@ def _model_config(name):
 def run_generation(args, world, rank, local):
     """Random-init model of the config's architecture (N(0, 0.02), norms 1),
     compressed through neuralzip.setup + the GPU export, then greedy
-    generation at batch 1; the uncompressed model generates the same tokens
-    first and its first-step logits must equal the compressed model's bit
-    for bit."""
+    generation with KV cache and eager attention. An uncompressed copy of
+    the same model is timed alternately with the compressed one (medians of
+    `--gen-reps` runs each, so drift of the host or the GPU hits both
+    alike); both must generate the same tokens, and the first-step logits
+    must be equal bit for bit."""
+    import copy
+
     from transformers import AutoModelForCausalLM
 
     from neuralzip_b200.gpu.inference import NeuralZipRuntime, export_model_for_gpu
@@ -310,7 +318,8 @@ def run_generation(args, world, rank, local):
     torch.manual_seed(0)
     with torch.device(device):
         model = AutoModelForCausalLM.from_config(config, dtype=torch.bfloat16).eval()
-    prompt = torch.randint(config.vocab_size, (1, prompt_len), generator=torch.Generator().manual_seed(1)).to(device)
+    prompt = torch.randint(config.vocab_size, (args.batch, prompt_len),
+                           generator=torch.Generator().manual_seed(1)).to(device)
 
     def run(m, n):
         torch.cuda.synchronize(device)
@@ -322,7 +331,7 @@ def run_generation(args, world, rank, local):
         return out, time.perf_counter() - t0
 
     def generate(m):
-        """Tokens and seconds per generated token after the first (prefill
+        """Tokens and seconds per generation step after the first (prefill
         and per-call setup excluded by timing a one-token call too)."""
         out, full = run(m, new_tokens)
         _, one = run(m, 1)
@@ -330,46 +339,58 @@ def run_generation(args, world, rank, local):
 
     with torch.no_grad():
         ref_logits = model(prompt, use_cache=False).logits.float().cpu()
-    generate(model)  # warm-up
-    ref_tokens, ref_s = generate(model)
+    uncompressed = copy.deepcopy(model)
     t0 = time.perf_counter()
     setup = NeuralZipSetup().build(model)
     exported = export_model_for_gpu(model, setup)
     prep_s = time.perf_counter() - t0
+    per_launch = "auto" if args.blocks_per_launch == 0 else args.blocks_per_launch
     runtime = NeuralZipRuntime.attach(model, exported, device=device, overlap=not args.no_overlap,
-                                      prefetch_depth=args.prefetch_depth)
+                                      prefetch_depth=args.prefetch_depth, blocks_per_launch=per_launch)
     with torch.no_grad():
         logits = model(prompt, use_cache=False).logits.float().cpu()
     identical = bool(torch.equal(logits.view(torch.int32), ref_logits.view(torch.int32)))
+    generate(uncompressed)  # warm-up
     generate(model)
-    tokens, comp_s = generate(model)
-    # Per-token decode work: one decode of every block.
+    ref_times, comp_times = [], []
+    for _ in range(args.gen_reps):
+        ref_tokens, t = generate(uncompressed)
+        ref_times.append(t)
+        tokens, t = generate(model)
+        comp_times.append(t)
+    ref_s, comp_s = statistics.median(ref_times), statistics.median(comp_times)
+    # Per-step decode work: one decode of every unit, as the schedule launches it.
     decode_ms = []
     stream = torch.cuda.current_stream(device)
     for _ in range(3):
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record(stream)
-        for name in exported.block_order:
-            runtime._decode_block(name)
+        for unit in range(len(runtime._units)):
+            runtime._decode_unit(unit, stream)
         b.record(stream)
         torch.cuda.synchronize(device)
         decode_ms.append(a.elapsed_time(b))
     decoded = sum(g.encoded.numel * g.encoded.dtype.element_size for g in exported.groups)
     if rank == 0:
         print(json.dumps({
-            "metric": "batch-1 greedy generation tok/s, compressed weights decoded per layer per token",
-            "value": round(1.0 / comp_s, 3), "unit": "tok/s", "n_gpus": 1, "higher_is_better": True,
-            "workload": args.workload, "uncompressed_tok_s": round(1.0 / ref_s, 3),
-            "ratio_vs_uncompressed": round(ref_s / comp_s, 4), "tokens_identical": bool(torch.equal(tokens, ref_tokens)),
+            "metric": f"batch-{args.batch} greedy generation tok/s, compressed weights decoded per layer per step",
+            "value": round(args.batch / comp_s, 3), "unit": "tok/s", "n_gpus": 1, "higher_is_better": True,
+            "workload": args.workload, "uncompressed_tok_s": round(args.batch / ref_s, 3),
+            "ratio_vs_uncompressed": round(ref_s / comp_s, 4),
+            "ratio_runs": [round(r / c, 4) for r, c in zip(ref_times, comp_times)],
+            "tokens_identical": bool(torch.equal(tokens, ref_tokens)),
             "first_step_logits_bitwise": identical, "overlap": runtime.overlap,
-            "prefetch_depth": runtime.prefetch_depth,
-            "decode_all_blocks_ms": round(min(decode_ms), 3),
+            "prefetch_depth": runtime.prefetch_depth, "blocks_per_launch": runtime.blocks_per_launch,
+            "launch_units": len(runtime._units),
+            "decode_per_step_ms": round(min(decode_ms), 3),
             "decode_gbs": round(decoded / (min(decode_ms) * 1e-3) / 1e9, 1),
             "compressed_weights": len({b.tensor_name for b in exported.bindings}), "prep_s": round(prep_s, 1),
-            "config": {"workload": args.workload, "prompt": prompt_len, "new_tokens": new_tokens,
-                       "attn": "eager", "kv_cache": True,
-                       "timing": "(t(new_tokens) - t(1)) / (new_tokens - 1): prefill excluded"},
+            "config": {"workload": args.workload, "batch": args.batch, "prompt": prompt_len,
+                       "new_tokens": new_tokens, "attn": "eager", "kv_cache": True,
+                       "timing": "(t(new_tokens) - t(1)) / (new_tokens - 1): prefill excluded; "
+                                 f"median of {args.gen_reps} runs alternating with the uncompressed model"},
         }))
+
 
 def main():
     args = parse_args()

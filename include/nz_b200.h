@@ -245,6 +245,39 @@ int nz_decode_occupancy(const nz_dtype* dtype, uint32_t warps_per_cta,
 /* Dynamic shared memory one CTA of nz_decode_launch uses. */
 int nz_decode_smem_bytes(uint32_t warps_per_cta, uint32_t* bytes);
 
+/* ---- host: decode schedule ----------------------------------------------- */
+
+/* The runtime's per-block decode as one C call per forward pre-hook.
+ * Replaces NeuralZipRuntime._decode_block / _install's hooks
+ * (neuralzip/gpu/inference.py:476-493), which decode each block on the
+ * current stream right before it runs; the schedule adds units of
+ * consecutive blocks per launch and, with depth > 1, an overlapped decode
+ * on `side_stream` into depth rotating workspace slots (unit u uses slot
+ * u % depth), ordered against the compute stream by CUDA events only.
+ * `launches` holds the nz_launch descriptors of all units, unit u owning
+ * [unit_first[u], unit_first[u + 1]); the device arrays they point to must
+ * outlive the schedule. Create it with the device of the launches current.
+ * A schedule is not thread-safe: one forward at a time. */
+typedef struct nz_schedule nz_schedule;
+int nz_schedule_create(const nz_launch* launches, const uint32_t* unit_first,
+                       uint32_t n_units, uint32_t depth, void* side_stream,
+                       nz_schedule** out);
+int nz_schedule_destroy(nz_schedule* schedule);
+/* Forward pre-hook of a block of `unit` (is_head: its first block): waits
+ * for the unit's side-stream decode, or decodes the unit on compute_stream
+ * when none is pending and the slot does not hold it (always for a head);
+ * a head then starts the side-stream decode of the following units whose
+ * slots are free. */
+int nz_schedule_enter(nz_schedule* schedule, uint32_t unit, uint32_t is_head,
+                      void* compute_stream);
+/* Decodes a whole unit on `stream` after every pending side decode. */
+int nz_schedule_decode_unit(nz_schedule* schedule, uint32_t unit, void* stream);
+/* Makes `stream` wait for every pending side decode. */
+int nz_schedule_drain(nz_schedule* schedule, void* stream);
+/* Records what a unit's slot holds after a decode done outside the
+ * schedule: the whole unit (whole = 1) or only part of it (0). */
+int nz_schedule_mark(nz_schedule* schedule, uint32_t unit, uint32_t whole);
+
 /* ---- errors ------------------------------------------------------------ */
 
 /* Copies the calling thread's last error message (NUL-terminated). */

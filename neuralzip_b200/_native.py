@@ -75,7 +75,8 @@ EXPORTS = (
     "nz_codebook_lut", "nz_huff0_build", "nz_huff0_read", "nz_pack_bound", "nz_pack_chunk",
     "nz_pack_many", "nz_split_lanes", "nz_exponent_histograms", "nz_count_tokens", "nz_mixed_encode", "nz_mixed_decode",
     "nz_huff0_encode", "nz_huff0_decode", "nz_decode_launch", "nz_decode_occupancy", "nz_decode_smem_bytes",
-    "nz_last_error",
+    "nz_schedule_create", "nz_schedule_destroy", "nz_schedule_enter", "nz_schedule_decode_unit",
+    "nz_schedule_drain", "nz_schedule_mark", "nz_last_error",
     "nz_abi_version",
 )
 
@@ -130,6 +131,12 @@ def _declare(lib):
         "nz_huff0_decode": [c.c_void_p, c.c_void_p, c.c_uint64, c.c_void_p, c.c_uint64],
         "nz_decode_launch": [c.POINTER(Launch), c.c_void_p],
         "nz_decode_occupancy": [c.POINTER(Dtype), c.c_uint32, u32p],
+        "nz_schedule_create": [c.POINTER(Launch), u32p, c.c_uint32, c.c_uint32, c.c_void_p, c.POINTER(c.c_void_p)],
+        "nz_schedule_destroy": [c.c_void_p],
+        "nz_schedule_enter": [c.c_void_p, c.c_uint32, c.c_uint32, c.c_void_p],
+        "nz_schedule_decode_unit": [c.c_void_p, c.c_uint32, c.c_void_p],
+        "nz_schedule_drain": [c.c_void_p, c.c_void_p],
+        "nz_schedule_mark": [c.c_void_p, c.c_uint32, c.c_uint32],
         "nz_decode_smem_bytes": [c.c_uint32, u32p],
         "nz_last_error": [c.c_char_p, c.c_size_t],
         "nz_abi_version": [],
@@ -370,6 +377,44 @@ def decode_occupancy(dt, warps_per_cta):
     out = ctypes.c_uint32()
     check(lib.nz_decode_occupancy(ctypes.byref(dt), int(warps_per_cta), ctypes.byref(out)))
     return out.value
+
+
+class Schedule:
+    """Owns an nz_schedule (the native per-block decode schedule)."""
+
+    def __init__(self, unit_launches, depth, side_stream_handle):
+        lib = load()
+        launches = [launch for unit in unit_launches for launch in unit]
+        first = [0]
+        for unit in unit_launches:
+            first.append(first[-1] + len(unit))
+        array = (Launch * max(1, len(launches)))(*launches)
+        first_array = (ctypes.c_uint32 * len(first))(*first)
+        handle = ctypes.c_void_p()
+        check(lib.nz_schedule_create(array, first_array, len(unit_launches), int(depth),
+                                     ctypes.c_void_p(int(side_stream_handle) or None), ctypes.byref(handle)))
+        self.handle = handle
+        self._lib = lib
+        self.enter_fn = lib.nz_schedule_enter  # bound once: the hook's only call
+
+    def enter(self, unit, head, stream_handle):
+        status = self.enter_fn(self.handle, unit, head, stream_handle)
+        if status:
+            check(status)
+
+    def decode_unit(self, unit, stream_handle):
+        check(self._lib.nz_schedule_decode_unit(self.handle, int(unit), ctypes.c_void_p(int(stream_handle) or None)))
+
+    def drain(self, stream_handle):
+        check(self._lib.nz_schedule_drain(self.handle, ctypes.c_void_p(int(stream_handle) or None)))
+
+    def mark(self, unit, whole):
+        check(self._lib.nz_schedule_mark(self.handle, int(unit), int(bool(whole))))
+
+    def close(self):
+        if self.handle:
+            self._lib.nz_schedule_destroy(self.handle)
+            self.handle = ctypes.c_void_p()
 
 
 def decode_launch(launch, stream_handle):

@@ -444,17 +444,6 @@ void run_jobs(uint64_t count, int threads, const std::function<void(uint64_t)>& 
 using nz::Error;
 using nz::fail;
 
-#define NZ_GUARD(...)                                               \
-    try {                                                            \
-        __VA_ARGS__;                                                        \
-        return NZ_OK;                                                \
-    } catch (const Error& e) {                                       \
-        return fail(e.status, e.what());                             \
-    } catch (const std::bad_alloc&) {                                \
-        return fail(NZ_ERUNTIME, "Out of host memory.");             \
-    } catch (const std::exception& e) {                              \
-        return fail(NZ_ERUNTIME, e.what());                          \
-    }
 
 extern "C" {
 

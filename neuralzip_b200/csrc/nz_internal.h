@@ -5,6 +5,7 @@
 
 #include <cstdint>
 #include <functional>
+#include <new>
 #include <stdexcept>
 #include <string>
 #include <vector>
@@ -71,3 +72,17 @@ std::vector<uint8_t> write_huff0_header(const uint8_t* lengths, uint32_t nsym);
 void huffman_lengths(const uint64_t* counts, uint32_t nsym, uint32_t max_bits, uint8_t* lengths);
 
 }  // namespace nz
+
+// Body of a C-ABI entry point: runs the statements, returns NZ_OK, and turns
+// exceptions into a status code plus the thread-local message.
+#define NZ_GUARD(...)                                        \
+    try {                                                    \
+        __VA_ARGS__;                                         \
+        return NZ_OK;                                        \
+    } catch (const nz::Error& e) {                           \
+        return nz::fail(e.status, e.what());                 \
+    } catch (const std::bad_alloc&) {                        \
+        return nz::fail(NZ_ERUNTIME, "Out of host memory."); \
+    } catch (const std::exception& e) {                      \
+        return nz::fail(NZ_ERUNTIME, e.what());              \
+    }

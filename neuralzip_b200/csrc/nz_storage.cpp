@@ -273,15 +273,6 @@ void huff0_decode(const Codebook& cb, const uint8_t* data, uint64_t size, uint8_
 
 using nz::Error;
 
-#define NZ_GUARD(...)                                    \
-    try {                                                \
-        __VA_ARGS__;                                     \
-        return NZ_OK;                                    \
-    } catch (const Error& e) {                           \
-        return nz::fail(e.status, e.what());             \
-    } catch (const std::exception& e) {                  \
-        return nz::fail(NZ_ERUNTIME, e.what());          \
-    }
 
 extern "C" {
 

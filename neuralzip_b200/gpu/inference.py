@@ -22,7 +22,7 @@ from __future__ import annotations
 import functools
 from collections import defaultdict
 from dataclasses import dataclass, field
-from functools import partial
+import weakref
 
 import numpy as np
 import torch
@@ -474,56 +474,103 @@ class _UploadedGroup:
         return self.group.layout
 
 
+def _current_stream_handle(index):
+    """Raw cudaStream_t of torch's current stream on device `index`."""
+    return torch.cuda.current_stream(index).cuda_stream
+
+
+if hasattr(torch._C, "_cuda_getCurrentRawStream"):
+    _current_stream_handle = torch._C._cuda_getCurrentRawStream  # noqa: F811  (same value, no Stream object)
+
+
+def _plan_units(exported, blocks_per_launch):
+    """Consecutive blocks decoded by one launch: fixed-size runs, or with
+    "auto" greedy runs whose decoded bytes stay within the largest block's."""
+    blocks = exported.block_order
+    if blocks_per_launch != "auto":
+        per_unit = max(1, int(blocks_per_launch))
+        return [tuple(blocks[i:i + per_unit]) for i in range(0, len(blocks), per_unit)]
+    size = defaultdict(int)
+    for group in exported.groups:
+        size[group.block_name] += group.encoded.numel * group.encoded.dtype.element_size
+    limit = max(size.values(), default=0)
+    units, current, total = [], [], 0
+    for name in blocks:
+        if current and total + size[name] > limit:
+            units.append(tuple(current))
+            current, total = [], 0
+        current.append(name)
+        total += size[name]
+    if current:
+        units.append(tuple(current))
+    return units
+
+
 class NeuralZipRuntime:
     """Runtime attached to one model on one CUDA device.
 
-    With ``overlap`` (the default when a model has two or more blocks) every
-    dtype gets ``prefetch_depth`` workspaces (2 = ping-pong): block i decodes
-    into buffer i % depth, and while block i runs, blocks i + 1 ..
-    i + depth - 1 are already being decoded on a side stream. The two streams
-    are ordered with CUDA events only: the compute stream waits for "block i
-    decoded" before block i runs, and the side stream waits for "everything
-    before block i enqueued" before it reuses a buffer, which covers the
-    buffer's previous reader (a prefetch whose buffer is still used by the
-    current or a later block is skipped and done when that block is
-    reached). A block reached out of order, and the direct ``_decode_block``
-    / ``materialized_weights`` calls, first drain pending side decodes and
-    then decode on the current stream, as the reference does
-    (neuralzip/gpu/inference.py:476-509). ``workspaces[dtype]`` covers all
-    buffers."""
+    Blocks are decoded in units of consecutive blocks: ``blocks_per_launch``
+    blocks (1 decodes block by block as the reference does), or with "auto"
+    (the default) as many as fit in the size of the largest block, so the
+    workspace is no larger than with single blocks. One launch per dtype
+    covers a unit, and the blocks of a unit lie side by side in one
+    workspace slot. Fewer, larger launches cost less host time per token and
+    lose less to the start and end of each launch.
 
-    def __init__(self, model, exported, device, *, overlap=True, prefetch_depth=2):
+    With ``overlap`` (the default when there are two or more units) every
+    dtype gets ``prefetch_depth`` slots (2 = ping-pong): unit k decodes into
+    slot k % depth, and while unit k runs, units k + 1 .. k + depth - 1 are
+    already being decoded on a side stream. The two streams are ordered with
+    CUDA events only: the compute stream waits for "unit k decoded" before
+    unit k runs, and the side stream waits for "everything before unit k
+    enqueued" before it reuses a slot, which covers the slot's previous
+    reader (a prefetch whose slot is still used by the current or a later
+    unit is skipped and done when that unit is reached).
+
+    The first block of a unit decodes it (or waits for its prefetch); the
+    other blocks only check that their unit is the one in the slot. A block
+    reached out of order decodes its unit first; the direct
+    ``_decode_block`` / ``materialized_weights`` calls drain pending side
+    decodes and decode one block on the current stream, as the reference
+    does (neuralzip/gpu/inference.py:476-509). ``workspaces[dtype]`` covers
+    all slots."""
+
+    def __init__(self, model, exported, device, *, overlap=True, prefetch_depth=2, blocks_per_launch="auto"):
         self.model = model
         self.export = exported
         self.device = torch.device(device)
         self._decoder = gpu_decoder.default_decoder()
         self._hook_handles = []
-        blocks = exported.block_order
-        n = len(blocks)
+        self._units = _plan_units(exported, blocks_per_launch)
+        self.blocks_per_launch = blocks_per_launch
+        n = len(self._units)
         self.overlap = bool(overlap) and n > 1
         depth = max(2, int(prefetch_depth)) if self.overlap else 1
         self.prefetch_depth = depth
-        self._block_index = {name: i for i, name in enumerate(blocks)}
-        self._parity = {name: i % depth for i, name in enumerate(blocks)}
-        # The block that used the same buffer last before each block (cyclic).
-        self._prev_user = {}
-        for i, name in enumerate(blocks):
-            j = (i - 1) % n
-            while j % depth != i % depth and j != i:
-                j = (j - 1) % n
-            self._prev_user[name] = blocks[j]
-        self._buffer_elems = dict(exported.workspace_sizes)
+        self._unit_of = {name: k for k, unit in enumerate(self._units) for name in unit}
+        self._slot = [k % depth for k in range(n)]
+        # Workspace: each block's extent per dtype, blocks of a unit side by side.
+        extent = defaultdict(int)
+        for group in exported.groups:
+            key = (group.block_name, group.encoded.dtype.torch_dtype)
+            extent[key] = max(extent[key], group.workspace_offset + group.encoded.numel)
+        dtypes = tuple(dict.fromkeys(group.encoded.dtype.torch_dtype for group in exported.groups))
+        self._block_base = {}
+        slot_elems = defaultdict(int)
+        for unit in self._units:
+            for dtype in dtypes:
+                size = DTYPES[dtype].element_size
+                cursor = 0
+                for name in unit:
+                    self._block_base[(name, dtype)] = cursor
+                    cursor = _aligned(cursor + extent.get((name, dtype), 0), size)
+                slot_elems[dtype] = max(slot_elems[dtype], cursor)
+        self._slot_elems = dict(slot_elems)
         self.workspaces = {
             dtype: torch.empty(size * depth, dtype=dtype, device=self.device)
-            for dtype, size in exported.workspace_sizes.items()
+            for dtype, size in self._slot_elems.items()
         }
         self._side = torch.cuda.Stream(device=self.device) if self.overlap else None
-        self._pending = {}
-        # Reused events per block: "buffer free" (compute) and "decoded" (side).
-        self._free_events = {name: torch.cuda.Event() for name in blocks} if self.overlap else {}
-        self._done_events = {name: torch.cuda.Event() for name in blocks} if self.overlap else {}
-        self._ahead = {name: tuple(blocks[(i + d) % n] for d in range(1, min(depth, n)))
-                       for i, name in enumerate(blocks)}
         # Decode tables: one row of LUT_WORDS words per codebook id.
         book_ids = sorted({g.codebook_id for g in exported.groups if g.codebook.max_bits})
         self._lut_rows = {cid: row for row, cid in enumerate(book_ids)}
@@ -576,18 +623,28 @@ class NeuralZipRuntime:
         for item in uploaded:
             by_block[item.group.block_name].append(item)
         self._groups_by_block = {name: tuple(by_block[name]) for name in exported.block_order}
-        self._prepared_batches = {}
-        for name, items in self._groups_by_block.items():
-            per_dtype = defaultdict(list)
-            for item in items:
-                per_dtype[item.group.encoded.dtype.name].append(item.device)
-            self._prepared_batches[name] = tuple(
-                self._decoder.prepare_batch(batch) for batch in per_dtype.values()
-            )
+        self._prepared_batches = {name: self._prepare(items) for name, items in self._groups_by_block.items()}
+        self._unit_batches = [
+            self._prepared_batches[unit[0]] if len(unit) == 1
+            else self._prepare([item for name in unit for item in self._groups_by_block[name]])
+            for unit in self._units
+        ]
+        # The schedule (native): slot residency, pending side decodes, events.
+        with torch.cuda.device(self.device):
+            self._schedule = _native.Schedule([[p.launch for p in batches] for batches in self._unit_batches],
+                                              depth, self._side.cuda_stream if self._side is not None else 0)
+        weakref.finalize(self, self._schedule.close)
         torch.cuda.synchronize(self.device)
 
+    def _prepare(self, items):
+        """One prepared launch per dtype over `items` (uploaded groups)."""
+        per_dtype = defaultdict(list)
+        for item in items:
+            per_dtype[item.group.encoded.dtype.name].append(item.device)
+        return tuple(self._decoder.prepare_batch(batch) for batch in per_dtype.values())
+
     @classmethod
-    def attach(cls, model, exported, *, device=None, overlap=True, prefetch_depth=2):
+    def attach(cls, model, exported, *, device=None, overlap=True, prefetch_depth=2, blocks_per_launch="auto"):
         if hasattr(model, RUNTIME_ATTRIBUTE):
             raise RuntimeError("This model already has a NeuralZip runtime.")
         if not exported.groups:
@@ -608,12 +665,14 @@ class NeuralZipRuntime:
             module._parameters.pop("weight", None)
             module.__dict__.pop("weight", None)
         model.to(device).eval()
-        runtime = cls(model, exported, device, overlap=overlap, prefetch_depth=prefetch_depth)
+        runtime = cls(model, exported, device, overlap=overlap, prefetch_depth=prefetch_depth,
+                      blocks_per_launch=blocks_per_launch)
         runtime._install()
         return runtime
 
     def _buffer_offset(self, block_name, dtype):
-        return self._parity[block_name] * self._buffer_elems[dtype]
+        slot = self._slot[self._unit_of[block_name]]
+        return slot * self._slot_elems[dtype] + self._block_base[(block_name, dtype)]
 
     def _binding_view(self, block_name, dtype, binding):
         offset = binding.workspace_offset + self._buffer_offset(block_name, dtype)
@@ -625,18 +684,37 @@ class NeuralZipRuntime:
                 for binding in item.group.bindings:
                     _binding_module(self.model, binding).__dict__["weight"] = self._binding_view(
                         name, item.group.encoded.dtype.torch_dtype, binding)
-        hook = self._pre_hook if self.overlap else self._decode_block
+        heads = {unit[0] for unit in self._units}
         for block_name in self.export.block_order:
-            handle = _decode_hook_module(self.model, block_name).register_forward_pre_hook(
-                partial(hook, block_name), prepend=True)
+            hook = self._make_hook(self._unit_of[block_name], int(block_name in heads))
+            handle = _decode_hook_module(self.model, block_name).register_forward_pre_hook(hook, prepend=True)
             self._hook_handles.append(handle)
         setattr(self.model, RUNTIME_ATTRIBUTE, self)
 
+    def _make_hook(self, unit, head):
+        """Forward pre-hook of one block: one native call
+        (nz_schedule_enter) on the current stream."""
+        enter, handle, index = self._schedule.enter_fn, self._schedule.handle, self.device.index
+
+        def hook(_module, _args):
+            status = enter(handle, unit, head, _current_stream_handle(index))
+            if status:
+                _native.check(status)
+
+        return hook
+
+    def _pre_hook(self, block_name, _module=None, _args=None):
+        """Runs the forward pre-hook of `block_name` by hand."""
+        unit = self._unit_of[block_name]
+        self._make_hook(unit, int(self._units[unit][0] == block_name))(_module, _args)
+
     def _drain(self, stream):
         """Makes `stream` wait for every pending side-stream decode."""
-        for event in self._pending.values():
-            stream.wait_event(event)
-        self._pending.clear()
+        self._schedule.drain(stream.cuda_stream)
+
+    def _decode_unit(self, unit, stream):
+        """Decodes a whole unit on `stream` (after pending side decodes)."""
+        self._schedule.decode_unit(unit, stream.cuda_stream)
 
     def _decode_block(self, block_name, _module=None, _args=None):
         """Decodes one block on the current stream (reference semantics)."""
@@ -644,40 +722,12 @@ class NeuralZipRuntime:
         self._drain(stream)
         for prepared in self._prepared_batches[block_name]:
             self._decoder.decode_batch(prepared, stream)
-
-    def _pre_hook(self, block_name, _module=None, _args=None):
-        """Forward pre-hook of the overlapped schedule."""
-        compute = torch.cuda.current_stream(self.device)
-        event = self._pending.pop(block_name, None)
-        if event is None:
-            self._decode_block(block_name)
-        else:
-            compute.wait_event(event)
-        index = self._block_index
-        n = len(index)
-        here = index[block_name]
-        free = None
-        for following in self._ahead[block_name]:
-            if following in self._pending:
-                continue
-            # The buffer's previous reader must already be enqueued, i.e. lie
-            # before this block; a reader in [this block, following) has not run.
-            prev = index[self._prev_user[following]]
-            if (prev - here) % n < (index[following] - here) % n:
-                break
-            if free is None:
-                free = self._free_events[block_name]
-                free.record(compute)
-                self._side.wait_event(free)
-            for prepared in self._prepared_batches[following]:
-                self._decoder.decode_batch(prepared, self._side)
-            done = self._done_events[following]
-            done.record(self._side)
-            self._pending[following] = done
+        unit = self._unit_of[block_name]
+        self._schedule.mark(unit, len(self._units[unit]) == 1)
 
     def check_status(self):
         """Raises if any decode launch reported a corrupt table."""
-        for batches in self._prepared_batches.values():
+        for batches in list(self._prepared_batches.values()) + list(self._unit_batches):
             for prepared in batches:
                 self._decoder.check_status(prepared)
 

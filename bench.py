@@ -156,7 +156,8 @@ def max_over_ranks(value, world):
         return value
     import torch.distributed as dist
 
-    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    device = "cuda" if dist.get_backend() == "nccl" else "cpu"
+    t = torch.tensor([value], dtype=torch.float64, device=device)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
 
@@ -515,7 +516,7 @@ def main():
             traffic = int(per_elem * main_batch.elements)
 
     cpu = None
-    if rank == 0 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:  # the CPU baseline is an N=1 figure
         from oracle import oracle as O
 
         if O.ref_available():

@@ -594,6 +594,11 @@ class NeuralZipRuntime:
         for placed in offsets:
             for start, data in placed.values():
                 host[start:start + len(data)] = np.frombuffer(data, dtype=np.uint8)
+        # Byte range of each group's arrays in the arena (groups are placed in order).
+        self.arena_ranges = tuple(
+            (min(start for start, _ in placed.values()), max(start + len(data) for start, data in placed.values()))
+            for placed in offsets)
+        self.arena_host = host
         self.arena = torch.from_numpy(host).to(self.device)
         base = self.arena.data_ptr()
         lut_base = self.decode_tables.data_ptr()

@@ -58,8 +58,11 @@ __device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
         asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
 
+// Streaming 16-byte store of decoded elements (evict-first in L2: they are
+// not read again by this kernel, and L2 keeps the prefetched inputs instead).
 __device__ __forceinline__ void stg_u4(void* p, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
-    *reinterpret_cast<uint4*>(p) = make_uint4(a, b, c, d);
+    asm volatile("st.global.cs.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(a), "r"(b), "r"(c), "r"(d)
+                 : "memory");
 }
 
 // MSB-first window over 32-bit words (bit 31 earliest). The valid bits are

@@ -237,6 +237,15 @@ typedef struct nz_launch {
 } nz_launch;
 int nz_decode_launch(const nz_launch* launch, void* cuda_stream);
 
+/* Several launches (e.g. one per dtype of a block) as one step on
+ * `cuda_stream`: the launch with the most warps runs alone on that stream,
+ * then the others run side by side on side streams of this library, and
+ * the stream waits for all of them. Small launches are latency-bound (one
+ * tile per warp), so running them together roughly halves their time. No
+ * reference counterpart (the reference launches each layout in turn,
+ * neuralzip/gpu/inference.py:491-493). */
+int nz_decode_launch_many(const nz_launch* launches, uint32_t count,
+                          void* cuda_stream);
 /* Resident CTAs per SM of the decode kernel for `dtype` at warps_per_cta
  * (the CUDA occupancy calculator on the current device; no reference
  * counterpart: the reference sizes its grid per group, decoder.py:89-119). */

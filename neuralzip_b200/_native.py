@@ -74,7 +74,7 @@ EXPORTS = (
     "nz_export_code_table", "nz_codebook_create", "nz_codebook_destroy", "nz_codebook_info",
     "nz_codebook_lut", "nz_huff0_build", "nz_huff0_read", "nz_pack_bound", "nz_pack_chunk",
     "nz_pack_many", "nz_split_lanes", "nz_exponent_histograms", "nz_count_tokens", "nz_mixed_encode", "nz_mixed_decode",
-    "nz_huff0_encode", "nz_huff0_decode", "nz_decode_launch", "nz_decode_occupancy", "nz_decode_smem_bytes",
+    "nz_huff0_encode", "nz_huff0_decode", "nz_decode_launch", "nz_decode_launch_many", "nz_decode_occupancy", "nz_decode_smem_bytes",
     "nz_schedule_create", "nz_schedule_destroy", "nz_schedule_enter", "nz_schedule_decode_unit",
     "nz_schedule_drain", "nz_schedule_mark", "nz_last_error",
     "nz_abi_version",
@@ -131,6 +131,7 @@ def _declare(lib):
         "nz_huff0_decode": [c.c_void_p, c.c_void_p, c.c_uint64, c.c_void_p, c.c_uint64],
         "nz_decode_launch": [c.POINTER(Launch), c.c_void_p],
         "nz_decode_occupancy": [c.POINTER(Dtype), c.c_uint32, u32p],
+        "nz_decode_launch_many": [c.POINTER(Launch), c.c_uint32, c.c_void_p],
         "nz_schedule_create": [c.POINTER(Launch), u32p, c.c_uint32, c.c_uint32, c.c_void_p, c.POINTER(c.c_void_p)],
         "nz_schedule_destroy": [c.c_void_p],
         "nz_schedule_enter": [c.c_void_p, c.c_uint32, c.c_uint32, c.c_void_p],
@@ -415,6 +416,14 @@ class Schedule:
         if self.handle:
             self._lib.nz_schedule_destroy(self.handle)
             self.handle = ctypes.c_void_p()
+
+
+def decode_launch_many(launches, stream_handle):
+    """Enqueues several launches as one step on a CUDA stream handle: the
+    largest on the stream, the others on the library's side streams."""
+    lib = load()
+    array = (Launch * len(launches))(*launches)
+    check(lib.nz_decode_launch_many(array, len(launches), ctypes.c_void_p(int(stream_handle) or None)))
 
 
 def decode_launch(launch, stream_handle):

@@ -29,6 +29,7 @@
 
 #include <mutex>
 #include <string>
+#include <vector>
 
 namespace {
 
@@ -408,6 +409,46 @@ cudaError_t occupancy_nw(uint32_t nw, int* ctas) {
     }
 }
 
+// Side streams of nz_decode_launch_many, per device, created on first use
+// and kept for the life of the process (with their fork/join events).
+struct AuxStreams {
+    std::mutex lock;
+    std::vector<cudaStream_t> streams;
+    std::vector<cudaEvent_t> join;
+    cudaEvent_t fork = nullptr;
+};
+
+int aux_streams(uint32_t needed, AuxStreams** out) {
+    static std::mutex registry_lock;
+    static std::vector<AuxStreams*> per_device;
+    int device = 0;
+    cudaError_t err = cudaGetDevice(&device);
+    if (err != cudaSuccess) return nz::fail(NZ_ECUDA, std::string("cudaGetDevice: ") + cudaGetErrorString(err));
+    AuxStreams* aux;
+    {
+        std::lock_guard<std::mutex> hold(registry_lock);
+        if (per_device.size() <= static_cast<size_t>(device)) per_device.resize(device + 1, nullptr);
+        if (!per_device[device]) per_device[device] = new AuxStreams();
+        aux = per_device[device];
+    }
+    std::lock_guard<std::mutex> hold(aux->lock);
+    if (!aux->fork) {
+        err = cudaEventCreateWithFlags(&aux->fork, cudaEventDisableTiming);
+        if (err != cudaSuccess) return nz::fail(NZ_ECUDA, std::string("cudaEventCreate: ") + cudaGetErrorString(err));
+    }
+    while (aux->streams.size() < needed) {
+        cudaStream_t s = nullptr;
+        cudaEvent_t e = nullptr;
+        err = cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking);
+        if (err == cudaSuccess) err = cudaEventCreateWithFlags(&e, cudaEventDisableTiming);
+        if (err != cudaSuccess) return nz::fail(NZ_ECUDA, std::string("aux stream: ") + cudaGetErrorString(err));
+        aux->streams.push_back(s);
+        aux->join.push_back(e);
+    }
+    *out = aux;
+    return NZ_OK;
+}
+
 enum class Kind { kBf16, kFp16, kFp32, kNone };
 
 Kind kind_of(const nz_dtype& d) {
@@ -447,6 +488,43 @@ int nz_decode_occupancy(const nz_dtype* dtype, uint32_t warps_per_cta, uint32_t*
     if (err != cudaSuccess)
         return nz::fail(NZ_ECUDA, std::string("CUDA occupancy query failed: ") + cudaGetErrorString(err));
     *ctas_per_sm = static_cast<uint32_t>(ctas);
+    return NZ_OK;
+}
+
+int nz_decode_launch_many(const nz_launch* launches, uint32_t count, void* cuda_stream) {
+    if (count == 0) return NZ_OK;
+    if (!launches) return nz::fail(NZ_EVALUE, "Null launch descriptors.");
+    cudaStream_t stream = reinterpret_cast<cudaStream_t>(cuda_stream);
+    // The launch with the most warps runs alone on the caller's stream (it
+    // fills every SM); the others then run side by side, each on a side
+    // stream, so that small launches, which are latency-bound, share SMs.
+    uint32_t main = 0;
+    for (uint32_t i = 1; i < count; ++i)
+        if (launches[i].n_ctas * launches[i].warps_per_cta > launches[main].n_ctas * launches[main].warps_per_cta)
+            main = i;
+    if (count == 1) return nz_decode_launch(&launches[0], cuda_stream);
+    AuxStreams* aux = nullptr;
+    int rc = aux_streams(count - 1, &aux);
+    if (rc != NZ_OK) return rc;
+    std::lock_guard<std::mutex> hold(aux->lock);
+    rc = nz_decode_launch(&launches[main], cuda_stream);
+    if (rc != NZ_OK) return rc;
+    cudaError_t err = cudaEventRecord(aux->fork, stream);
+    if (err != cudaSuccess) return nz::fail(NZ_ECUDA, std::string("cudaEventRecord: ") + cudaGetErrorString(err));
+    uint32_t k = 0;
+    for (uint32_t i = 0; i < count; ++i) {
+        if (i == main) continue;
+        cudaStream_t side = aux->streams[k];
+        err = cudaStreamWaitEvent(side, aux->fork, 0);
+        if (err != cudaSuccess)
+            return nz::fail(NZ_ECUDA, std::string("cudaStreamWaitEvent: ") + cudaGetErrorString(err));
+        rc = nz_decode_launch(&launches[i], side);
+        if (rc != NZ_OK) return rc;
+        err = cudaEventRecord(aux->join[k], side);
+        if (err == cudaSuccess) err = cudaStreamWaitEvent(stream, aux->join[k], 0);
+        if (err != cudaSuccess) return nz::fail(NZ_ECUDA, std::string("stream join: ") + cudaGetErrorString(err));
+        ++k;
+    }
     return NZ_OK;
 }
 

@@ -54,11 +54,8 @@ int drain(nz_schedule& s, cudaStream_t stream) {
 }
 
 int launch_unit(nz_schedule& s, uint32_t unit, cudaStream_t stream) {
-    for (uint32_t i = s.first[unit]; i < s.first[unit + 1]; ++i) {
-        const int rc = nz_decode_launch(&s.launches[i], stream);
-        if (rc != NZ_OK) return rc;
-    }
-    return NZ_OK;
+    const uint32_t count = s.first[unit + 1] - s.first[unit];
+    return nz_decode_launch_many(s.launches.data() + s.first[unit], count, stream);
 }
 
 int decode_unit(nz_schedule& s, uint32_t unit, cudaStream_t stream) {

@@ -82,8 +82,7 @@ class HostDecoder:
                 rt.arena[lo:hi].copy_(self.host_arena[lo:hi], non_blocking=True)
                 self._loaded[i].record(self.h2d)
             self.compute.wait_event(self._loaded[i])
-            for prepared in batches:
-                rt._decoder.decode_batch(prepared, self.compute)
+            rt._decoder.decode_batches(batches, self.compute)
             self._decoded[i].record(self.compute)
             self.d2h.wait_event(self._decoded[i])
             with torch.cuda.stream(self.d2h):

@@ -230,6 +230,22 @@ class TileDecoder:
             elements=sum(g.numel for g in groups),
         )
 
+    def decode_batches(self, batches, stream=None):
+        """Enqueues several prepared batches (e.g. one per dtype of a block)
+        as one step on `stream`: the largest alone on the stream, then the
+        others side by side on the library's side streams, joined back
+        (nz_decode_launch_many)."""
+        batches = tuple(batches)
+        if not batches:
+            return ()
+        if stream is None:
+            stream = torch.cuda.current_stream(device=batches[0].device)
+        if len(batches) == 1:
+            _native.decode_launch(batches[0].launch, stream.cuda_stream)
+        else:
+            _native.decode_launch_many([b.launch for b in batches], stream.cuda_stream)
+        return tuple(out for b in batches for out in b.outputs)
+
     def decode_batch(self, prepared, stream=None):
         """Enqueues the decode on `stream` (default: torch's current stream)."""
         if stream is None:

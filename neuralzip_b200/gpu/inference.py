@@ -725,8 +725,7 @@ class NeuralZipRuntime:
         """Decodes one block on the current stream (reference semantics)."""
         stream = torch.cuda.current_stream(self.device)
         self._drain(stream)
-        for prepared in self._prepared_batches[block_name]:
-            self._decoder.decode_batch(prepared, stream)
+        self._decoder.decode_batches(self._prepared_batches[block_name], stream)
         unit = self._unit_of[block_name]
         self._schedule.mark(unit, len(self._units[unit]) == 1)
 

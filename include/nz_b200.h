@@ -209,31 +209,40 @@ typedef struct nz_work {
     uint32_t tile;
 } nz_work;
 
-/* One CTA: a contiguous range of works sharing one decode table. */
+/* Element layouts the decode kernel writes (nz_cta.layout): bf16 (sign
+ * moved under the exponent, byte 1 coded), fp16 (no reorder, byte 1 coded)
+ * and fp32 (sign moved, byte 3 coded); neuralzip/dtypes.py:23-83. */
+#define NZ_LAYOUT_BF16 0u
+#define NZ_LAYOUT_FP16 1u
+#define NZ_LAYOUT_FP32 2u
+
+/* One CTA: a contiguous range of works sharing one decode table and one
+ * element layout. */
 typedef struct nz_cta {
     uint32_t lut;        /* index into luts, or NZ_RAW_LUT */
     uint32_t begin;
     uint32_t end;
-    uint32_t lut_words;  /* words of the table to stage (<= NZ_LUT_WORDS) */
+    uint16_t lut_words;  /* words of the table to stage (<= NZ_LUT_WORDS) */
+    uint16_t layout;     /* NZ_LAYOUT_* of every group of the range */
 } nz_cta;
 
 /* Replaces CuPyDecoder.decode_batch (neuralzip/gpu/decoder.py:193-208) and
  * the kernel launch of decode_batched (neuralzip/gpu/cuda/decode.cu:323).
- * All arrays are device-resident; `luts` is a device array of device
+ * One launch decodes groups of any mix of layouts (each CTA names its
+ * own). All arrays are device-resident; `luts` is a device array of device
  * pointers to NZ_LUT_WORDS-word tables. `status` (device int32) receives a
- * nonzero code if a corrupt table made a lane give up; it is only written
- * on error. Asynchronous on `cuda_stream` (a cudaStream_t, NULL = legacy
- * default stream). warps_per_cta: 4, 8 or 16 (0 = default, 8). */
+ * nonzero code if a corrupt table made a lane give up (2) or a CTA named an
+ * unknown layout (3); it is only written on error. Asynchronous on
+ * `cuda_stream` (a cudaStream_t, NULL = legacy default stream).
+ * warps_per_cta: 4, 8 or 16 (0 = default, 8). */
 typedef struct nz_launch {
-    nz_dtype dtype;
     uint32_t warps_per_cta;
+    uint32_t n_ctas;
     uint64_t groups;  /* const nz_group* */
     uint64_t works;   /* const nz_work* */
     uint64_t ctas;    /* const nz_cta* */
     uint64_t luts;    /* const uint64_t* */
     uint64_t status;  /* int32_t* */
-    uint32_t n_ctas;
-    uint32_t pad;
 } nz_launch;
 int nz_decode_launch(const nz_launch* launch, void* cuda_stream);
 
@@ -246,11 +255,10 @@ int nz_decode_launch(const nz_launch* launch, void* cuda_stream);
  * neuralzip/gpu/inference.py:491-493). */
 int nz_decode_launch_many(const nz_launch* launches, uint32_t count,
                           void* cuda_stream);
-/* Resident CTAs per SM of the decode kernel for `dtype` at warps_per_cta
- * (the CUDA occupancy calculator on the current device; no reference
- * counterpart: the reference sizes its grid per group, decoder.py:89-119). */
-int nz_decode_occupancy(const nz_dtype* dtype, uint32_t warps_per_cta,
-                        uint32_t* ctas_per_sm);
+/* Resident CTAs per SM of the decode kernel at warps_per_cta (the CUDA
+ * occupancy calculator on the current device; no reference counterpart:
+ * the reference sizes its grid per group, decoder.py:89-119). */
+int nz_decode_occupancy(uint32_t warps_per_cta, uint32_t* ctas_per_sm);
 /* Dynamic shared memory one CTA of nz_decode_launch uses. */
 int nz_decode_smem_bytes(uint32_t warps_per_cta, uint32_t* bytes);
 

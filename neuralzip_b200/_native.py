@@ -30,6 +30,8 @@ LUT_WORDS = LUT_TREE + 2 * TREE_MAX_NODES
 MAX_CODE_BITS = 56
 BITS_PAD_WORDS = 16
 RAW_LUT = 0xFFFFFFFF
+ABI_VERSION = 3
+LAYOUT_BF16, LAYOUT_FP16, LAYOUT_FP32 = 0, 1, 2
 
 OK, EVALUE, ETYPE, EOVERFLOW, ERUNTIME, ECUDA = range(6)
 _ERRORS = {EVALUE: ValueError, ETYPE: TypeError, EOVERFLOW: OverflowError, ERUNTIME: RuntimeError,
@@ -58,16 +60,16 @@ class PackJob(ctypes.Structure):
 
 
 class Launch(ctypes.Structure):
-    _fields_ = [("dtype", Dtype), ("warps_per_cta", ctypes.c_uint32), ("groups", ctypes.c_uint64),
+    _fields_ = [("warps_per_cta", ctypes.c_uint32), ("n_ctas", ctypes.c_uint32), ("groups", ctypes.c_uint64),
                 ("works", ctypes.c_uint64), ("ctas", ctypes.c_uint64), ("luts", ctypes.c_uint64),
-                ("status", ctypes.c_uint64), ("n_ctas", ctypes.c_uint32), ("pad", ctypes.c_uint32)]
+                ("status", ctypes.c_uint64)]
 
 
 # Device descriptor records (numpy views of the C structs).
 GROUP_DTYPE = np.dtype([("bits", "<u8"), ("lens", "<u8"), ("tile_off", "<u8"), ("lanes", "<u8", (4,)),
                         ("out", "<u8"), ("numel", "<u4"), ("lut", "<u4")])
 WORK_DTYPE = np.dtype([("group", "<u4"), ("tile", "<u4")])
-CTA_DTYPE = np.dtype([("lut", "<u4"), ("begin", "<u4"), ("end", "<u4"), ("lut_words", "<u4")])
+CTA_DTYPE = np.dtype([("lut", "<u4"), ("begin", "<u4"), ("end", "<u4"), ("lut_words", "<u2"), ("layout", "<u2")])
 assert GROUP_DTYPE.itemsize == 72 and WORK_DTYPE.itemsize == 8 and CTA_DTYPE.itemsize == 16
 
 EXPORTS = (
@@ -100,7 +102,7 @@ def load():
             _build.build()
         lib = ctypes.CDLL(str(LIBRARY))
         _declare(lib)
-        if lib.nz_abi_version() != 1:
+        if lib.nz_abi_version() != ABI_VERSION:
             raise RuntimeError("libnzb200.so ABI version mismatch.")
         _lib = lib
         return lib
@@ -130,7 +132,7 @@ def _declare(lib):
         "nz_huff0_encode": [c.c_void_p, c.c_void_p, c.c_uint64, c.c_void_p, c.c_uint64, u64p],
         "nz_huff0_decode": [c.c_void_p, c.c_void_p, c.c_uint64, c.c_void_p, c.c_uint64],
         "nz_decode_launch": [c.POINTER(Launch), c.c_void_p],
-        "nz_decode_occupancy": [c.POINTER(Dtype), c.c_uint32, u32p],
+        "nz_decode_occupancy": [c.c_uint32, u32p],
         "nz_decode_launch_many": [c.POINTER(Launch), c.c_uint32, c.c_void_p],
         "nz_schedule_create": [c.POINTER(Launch), u32p, c.c_uint32, c.c_uint32, c.c_void_p, c.POINTER(c.c_void_p)],
         "nz_schedule_destroy": [c.c_void_p],
@@ -372,12 +374,19 @@ def decode_smem_bytes(warps_per_cta=8):
     return out.value
 
 
-def decode_occupancy(dt, warps_per_cta):
+def decode_occupancy(warps_per_cta):
     """Resident decode CTAs per SM on the current CUDA device."""
     lib = load()
     out = ctypes.c_uint32()
-    check(lib.nz_decode_occupancy(ctypes.byref(dt), int(warps_per_cta), ctypes.byref(out)))
+    check(lib.nz_decode_occupancy(int(warps_per_cta), ctypes.byref(out)))
     return out.value
+
+
+def layout_code(element_size, bit_reorder, mantissa_bits, exponent_bits, stream_id):
+    """NZ_LAYOUT_* of a DTypeSpec's GPU layout, or None if the kernel has none."""
+    return {(2, True, 7, 8, 1): LAYOUT_BF16, (2, False, 10, 5, 1): LAYOUT_FP16,
+            (4, True, 23, 8, 3): LAYOUT_FP32}.get(
+        (int(element_size), bool(bit_reorder), int(mantissa_bits), int(exponent_bits), int(stream_id)))
 
 
 class Schedule:

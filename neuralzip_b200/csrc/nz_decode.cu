@@ -199,28 +199,17 @@ __device__ __forceinline__ void merge_tail(uint8_t* out, const uint8_t* const* l
     }
 }
 
+// The works [begin, end) of one CTA, taken in turn by its NW warps, for
+// one element layout. `table` is the CTA's staged decode table.
 template <int ES, bool REORDER, int NW>
-__global__ void __launch_bounds__(NW * 32, (NW >= 16 ? 2 : (NW >= 8 ? 4 : 8)))
-    nz_tile_decode(const nz_group* __restrict__ groups, const nz_work* __restrict__ works,
-                   const nz_cta* __restrict__ ctas, const uint64_t* __restrict__ luts,
-                   int32_t* __restrict__ status) {
+__device__ __forceinline__ void decode_works(const nz_group* __restrict__ groups,
+                                             const nz_work* __restrict__ works, uint32_t begin,
+                                             uint32_t end, const uint32_t* __restrict__ table,
+                                             uint32_t* stage, int32_t* __restrict__ status) {
     using L = Layout<ES, REORDER>;
-    extern __shared__ __align__(16) uint32_t smem[];
-    uint32_t* table = smem;
     const uint32_t warp = threadIdx.x >> 5;
     const uint32_t lane = threadIdx.x & 31U;
-    uint32_t* stage = smem + NZ_LUT_WORDS + warp * kStageWordsPerWarp;
-
-    const nz_cta cta = ctas[blockIdx.x];
-    if (cta.lut != NZ_RAW_LUT) {
-        const uint4* src = reinterpret_cast<const uint4*>(luts[cta.lut]);
-        uint4* dst = reinterpret_cast<uint4*>(table);
-        const uint32_t n4 = (min(cta.lut_words, NZ_LUT_WORDS) + 3U) / 4U;  // tables hold NZ_LUT_WORDS
-        for (uint32_t i = threadIdx.x; i < n4; i += NW * 32) dst[i] = __ldg(src + i);
-    }
-    __syncthreads();
-
-    for (uint32_t w = cta.begin + warp; w < cta.end; w += NW) {
+    for (uint32_t w = begin + warp; w < end; w += NW) {
         const nz_work item = works[w];
         const nz_group& g = groups[item.group];
         const uint32_t numel = g.numel;
@@ -354,59 +343,84 @@ __global__ void __launch_bounds__(NW * 32, (NW >= 16 ? 2 : (NW >= 8 ? 4 : 8)))
     }
 }
 
-template <int ES, bool REORDER, int NW>
+constexpr int32_t kStatusBadLayout = 3;
+
+// One launch covers CTAs of every element layout: each CTA stages its
+// decode table and runs the body of its layout (uniform per CTA, so the
+// switch does not diverge).
+template <int NW>
+__global__ void __launch_bounds__(NW * 32, (NW >= 16 ? 2 : (NW >= 8 ? 4 : 8)))
+    nz_tile_decode(const nz_group* __restrict__ groups, const nz_work* __restrict__ works,
+                   const nz_cta* __restrict__ ctas, const uint64_t* __restrict__ luts,
+                   int32_t* __restrict__ status) {
+    extern __shared__ __align__(16) uint32_t smem[];
+    uint32_t* table = smem;
+    uint32_t* stage = smem + NZ_LUT_WORDS + (threadIdx.x >> 5) * kStageWordsPerWarp;
+
+    const nz_cta cta = ctas[blockIdx.x];
+    if (cta.lut != NZ_RAW_LUT) {
+        const uint4* src = reinterpret_cast<const uint4*>(luts[cta.lut]);
+        uint4* dst = reinterpret_cast<uint4*>(table);
+        const uint32_t n4 = (min(static_cast<uint32_t>(cta.lut_words), NZ_LUT_WORDS) + 3U) / 4U;
+        for (uint32_t i = threadIdx.x; i < n4; i += NW * 32) dst[i] = __ldg(src + i);
+    }
+    __syncthreads();
+    switch (cta.layout) {
+        case NZ_LAYOUT_BF16:
+            decode_works<2, true, NW>(groups, works, cta.begin, cta.end, table, stage, status);
+            break;
+        case NZ_LAYOUT_FP16:
+            decode_works<2, false, NW>(groups, works, cta.begin, cta.end, table, stage, status);
+            break;
+        case NZ_LAYOUT_FP32:
+            decode_works<4, true, NW>(groups, works, cta.begin, cta.end, table, stage, status);
+            break;
+        default:
+            if (threadIdx.x == 0 && status) *status = kStatusBadLayout;
+    }
+}
+
+template <int NW>
 constexpr size_t smem_bytes() {
     return (NZ_LUT_WORDS + NW * kStageWordsPerWarp) * sizeof(uint32_t);
 }
 
 // Opts the instantiation into its dynamic shared memory (once per process).
-template <int ES, bool REORDER, int NW>
+template <int NW>
 cudaError_t ensure_smem_attribute() {
     static std::once_flag once;
     static cudaError_t err = cudaSuccess;
     std::call_once(once, [&]() {
-        err = cudaFuncSetAttribute(nz_tile_decode<ES, REORDER, NW>,
-                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   static_cast<int>(smem_bytes<ES, REORDER, NW>()));
+        err = cudaFuncSetAttribute(nz_tile_decode<NW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   static_cast<int>(smem_bytes<NW>()));
     });
     return err;
 }
 
-template <int ES, bool REORDER, int NW>
+template <int NW>
 cudaError_t launch_one(const nz_launch& l, cudaStream_t stream) {
-    const cudaError_t attr_err = ensure_smem_attribute<ES, REORDER, NW>();
+    const cudaError_t attr_err = ensure_smem_attribute<NW>();
     if (attr_err != cudaSuccess) return attr_err;
-    nz_tile_decode<ES, REORDER, NW><<<l.n_ctas, NW * 32, smem_bytes<ES, REORDER, NW>(), stream>>>(
+    nz_tile_decode<NW><<<l.n_ctas, NW * 32, smem_bytes<NW>(), stream>>>(
         reinterpret_cast<const nz_group*>(l.groups), reinterpret_cast<const nz_work*>(l.works),
         reinterpret_cast<const nz_cta*>(l.ctas), reinterpret_cast<const uint64_t*>(l.luts),
         reinterpret_cast<int32_t*>(l.status));
     return cudaGetLastError();
 }
 
-template <int ES, bool REORDER>
 cudaError_t launch_nw(const nz_launch& l, cudaStream_t stream) {
     switch (l.warps_per_cta) {
-        case 4: return launch_one<ES, REORDER, 4>(l, stream);
-        case 16: return launch_one<ES, REORDER, 16>(l, stream);
-        default: return launch_one<ES, REORDER, 8>(l, stream);
+        case 4: return launch_one<4>(l, stream);
+        case 16: return launch_one<16>(l, stream);
+        default: return launch_one<8>(l, stream);
     }
 }
 
-template <int ES, bool REORDER, int NW>
+template <int NW>
 cudaError_t occupancy_one(int* ctas) {
-    const cudaError_t err = ensure_smem_attribute<ES, REORDER, NW>();
+    const cudaError_t err = ensure_smem_attribute<NW>();
     if (err != cudaSuccess) return err;
-    return cudaOccupancyMaxActiveBlocksPerMultiprocessor(ctas, nz_tile_decode<ES, REORDER, NW>, NW * 32,
-                                                         smem_bytes<ES, REORDER, NW>());
-}
-
-template <int ES, bool REORDER>
-cudaError_t occupancy_nw(uint32_t nw, int* ctas) {
-    switch (nw) {
-        case 4: return occupancy_one<ES, REORDER, 4>(ctas);
-        case 16: return occupancy_one<ES, REORDER, 16>(ctas);
-        default: return occupancy_one<ES, REORDER, 8>(ctas);
-    }
+    return cudaOccupancyMaxActiveBlocksPerMultiprocessor(ctas, nz_tile_decode<NW>, NW * 32, smem_bytes<NW>());
 }
 
 // Side streams of nz_decode_launch_many, per device, created on first use
@@ -449,18 +463,6 @@ int aux_streams(uint32_t needed, AuxStreams** out) {
     return NZ_OK;
 }
 
-enum class Kind { kBf16, kFp16, kFp32, kNone };
-
-Kind kind_of(const nz_dtype& d) {
-    if (d.elem_size == 2 && d.stream_id == 1 && d.reorder && d.mant_bits == 7 && d.exp_bits == 8)
-        return Kind::kBf16;
-    if (d.elem_size == 2 && d.stream_id == 1 && !d.reorder && d.mant_bits == 10 && d.exp_bits == 5)
-        return Kind::kFp16;
-    if (d.elem_size == 4 && d.stream_id == 3 && d.reorder && d.mant_bits == 23 && d.exp_bits == 8)
-        return Kind::kFp32;
-    return Kind::kNone;
-}
-
 }  // namespace
 
 extern "C" {
@@ -472,18 +474,16 @@ int nz_decode_smem_bytes(uint32_t warps_per_cta, uint32_t* bytes) {
     return NZ_OK;
 }
 
-int nz_decode_occupancy(const nz_dtype* dtype, uint32_t warps_per_cta, uint32_t* ctas_per_sm) {
-    if (!dtype || !ctas_per_sm) return nz::fail(NZ_EVALUE, "Null argument.");
-    if (warps_per_cta != 0 && warps_per_cta != 4 && warps_per_cta != 8 && warps_per_cta != 16)
-        return nz::fail(NZ_EVALUE, "warps_per_cta must be 4, 8 or 16.");
+int nz_decode_occupancy(uint32_t warps_per_cta, uint32_t* ctas_per_sm) {
+    if (!ctas_per_sm) return nz::fail(NZ_EVALUE, "Null argument.");
     int ctas = 0;
     cudaError_t err;
-    switch (kind_of(*dtype)) {
-        case Kind::kBf16: err = occupancy_nw<2, true>(warps_per_cta, &ctas); break;
-        case Kind::kFp16: err = occupancy_nw<2, false>(warps_per_cta, &ctas); break;
-        case Kind::kFp32: err = occupancy_nw<4, true>(warps_per_cta, &ctas); break;
-        default:
-            return nz::fail(NZ_EVALUE, "Unsupported GPU layout (bf16, fp16 and fp32 are decoded).");
+    switch (warps_per_cta) {
+        case 4: err = occupancy_one<4>(&ctas); break;
+        case 0:
+        case 8: err = occupancy_one<8>(&ctas); break;
+        case 16: err = occupancy_one<16>(&ctas); break;
+        default: return nz::fail(NZ_EVALUE, "warps_per_cta must be 4, 8 or 16.");
     }
     if (err != cudaSuccess)
         return nz::fail(NZ_ECUDA, std::string("CUDA occupancy query failed: ") + cudaGetErrorString(err));
@@ -537,15 +537,7 @@ int nz_decode_launch(const nz_launch* launch, void* cuda_stream) {
     if (l.warps_per_cta != 0 && l.warps_per_cta != 4 && l.warps_per_cta != 8 &&
         l.warps_per_cta != 16)
         return nz::fail(NZ_EVALUE, "warps_per_cta must be 4, 8 or 16.");
-    cudaStream_t stream = reinterpret_cast<cudaStream_t>(cuda_stream);
-    cudaError_t err;
-    switch (kind_of(l.dtype)) {
-        case Kind::kBf16: err = launch_nw<2, true>(l, stream); break;
-        case Kind::kFp16: err = launch_nw<2, false>(l, stream); break;
-        case Kind::kFp32: err = launch_nw<4, true>(l, stream); break;
-        default:
-            return nz::fail(NZ_EVALUE, "Unsupported GPU layout (bf16, fp16 and fp32 are decoded).");
-    }
+    const cudaError_t err = launch_nw(l, reinterpret_cast<cudaStream_t>(cuda_stream));
     if (err != cudaSuccess)
         return nz::fail(NZ_ECUDA, std::string("CUDA launch failed: ") + cudaGetErrorString(err));
     return NZ_OK;

@@ -32,7 +32,11 @@ from neuralzip_b200 import _native
 KERNEL_PATH = Path(__file__).resolve().parent.parent / "csrc" / "nz_decode.cu"
 WARPS_PER_CTA = 16
 SM_COUNT_DEFAULT = 148
-# A raw tile (no Huffman decode) takes about a quarter of a coded tile's time.
+# Cost of a coded tile relative to a pair-coded bf16 tile (measured on
+# config 2: fp16 bytes are singleton-coded, fewer bytes per lookup; fp32
+# tiles move twice the bytes). A raw tile (no Huffman decode) costs about a
+# quarter.
+WORK_WEIGHT = {_native.LAYOUT_BF16: 1.0, _native.LAYOUT_FP16: 2.0, _native.LAYOUT_FP32: 2.0}
 RAW_WORK_WEIGHT = 4
 
 
@@ -46,9 +50,9 @@ def shared_memory_bytes(warps_per_cta=WARPS_PER_CTA, max_elements=None):
     return _native.decode_smem_bytes(warps_per_cta)
 
 
-def _native_dtype(spec):
-    return _native.dtype_struct(spec.element_size, spec.bit_reorder, spec.mantissa_bits,
-                                spec.exponent_bits, spec.gpu_stream)
+def _layout_of(spec):
+    return _native.layout_code(spec.element_size, spec.bit_reorder, spec.mantissa_bits, spec.exponent_bits,
+                               spec.gpu_stream)
 
 
 @dataclass(frozen=True)
@@ -95,44 +99,55 @@ class TileDecoder:
         self._ctas_per_sm = {}
 
     # Reference hook: the staging policy decides the launch geometry.
-    def staging_policy(self, device_index, lut_works, layout=None):
-        """Launch geometry for a batch with ``lut_works[lut] = (works, raw)``
-        tiles per decode table: (warps per CTA, {lut: works per CTA}).
+    def staging_policy(self, device_index, key_works):
+        """Launch geometry for a batch with ``key_works[key] = (tiles,
+        layout, raw)`` per (layout, decode table): (warps per CTA,
+        {key: works per CTA}).
 
-        Every CTA stages one table and its warps take the CTA's works in
-        turn, so they get equal counts (+-1). The works per warp are the
+        Every CTA stages one table and runs one layout; its warps take the
+        CTA's works in turn, so they get equal counts (+-1). Tiles are
+        weighed by their cost relative to a pair-coded bf16 tile
+        (WORK_WEIGHT, RAW_WORK_WEIGHT), and the works per warp are the
         smallest count whose CTAs fit in one wave of resident CTAs: a launch
         then ends when its busiest warps do, instead of with a partial last
-        wave that leaves SMs idle. Small launches use narrower CTAs so that
-        every SM gets work."""
+        wave that leaves SMs idle. A launch with fewer tiles than one
+        16-warp CTA per SM uses narrower CTAs so that every SM gets work
+        (16-warp CTAs hold the most resident warps: 32 per SM against 24
+        and 16 for 8- and 4-warp CTAs, whose shared memory is mostly the
+        36 KB table)."""
         sms = self._sms(device_index)
-        total = sum(n for n, _ in lut_works.values())
+        total = sum(n for n, _, _ in key_works.values())
         nw = WARPS_PER_CTA
-        while nw > 4 and total < 2 * sms * nw:
+        while nw > 4 and total < sms * nw:
             nw //= 2
-        slots = self._occupancy(device_index, layout, nw) * sms
+        slots = self._occupancy(device_index, nw) * sms
 
-        def weight(raw):
-            return RAW_WORK_WEIGHT if raw else 1
+        def per_warp_of(layout, raw):
+            """Works per warp-unit of cost, as a divisor of the common count."""
+            return (WORK_WEIGHT[layout] * (1.0 / RAW_WORK_WEIGHT if raw else 1.0))
 
-        def ctas(per_warp):
-            return sum(-(-n // (nw * per_warp * weight(raw))) for n, raw in lut_works.values())
+        def plan(units):
+            return {key: max(1, int(round(nw * units / per_warp_of(layout, raw))))
+                    for key, (_, layout, raw) in key_works.items()}
 
-        per_warp = max(1, -(-total // (slots * nw)))
-        while ctas(per_warp) > slots:
-            per_warp += 1
-        return nw, {lut: nw * per_warp * weight(raw) for lut, (_, raw) in lut_works.items()}
+        def ctas(per_cta):
+            return sum(-(-n // per_cta[key]) for key, (n, _, _) in key_works.items())
 
-    def _occupancy(self, device_index, layout, nw):
+        cost = sum(n * per_warp_of(layout, raw) for n, layout, raw in key_works.values())
+        units = max(1, -(-int(cost) // (slots * nw)))
+        while ctas(plan(units)) > slots:
+            units += 1
+        return nw, plan(units)
+
+    def _occupancy(self, device_index, nw):
         """Resident CTAs per SM (CUDA occupancy calculator; shared memory
         allows 2, 3 and 4 CTAs of 16, 8 and 4 warps on a B200)."""
-        key = (device_index, layout, nw)
+        key = (device_index, nw)
         if key not in self._ctas_per_sm:
             fallback = {16: 2, 8: 3, 4: 4}[nw]
             try:
                 with torch.cuda.device(device_index):
-                    dt = _native.dtype_struct(*layout) if layout else _native.dtype_struct(2, True, 7, 8, 1)
-                    self._ctas_per_sm[key] = _native.decode_occupancy(dt, nw) or fallback
+                    self._ctas_per_sm[key] = _native.decode_occupancy(nw) or fallback
             except (RuntimeError, AssertionError, TypeError):
                 self._ctas_per_sm[key] = fallback
         return self._ctas_per_sm[key]
@@ -149,11 +164,8 @@ class TileDecoder:
         """Validates a GPUWeightGroup before any weight is removed
         (neuralzip/gpu/decoder.py:121-128): the dtype must have a tile
         kernel and the codebook a decode table."""
-        spec = group.encoded.dtype
         _native.load()
-        key = (spec.element_size, bool(spec.bit_reorder), spec.mantissa_bits, spec.exponent_bits,
-               spec.gpu_stream)
-        if key not in {(2, True, 7, 8, 1), (2, False, 10, 5, 1), (4, True, 23, 8, 3)}:
+        if _layout_of(group.encoded.dtype) is None:
             raise ValueError("The GPU decoder has no kernel for this dtype layout.")
         if group.codebook.max_bits and group.codebook.decode_lut is None:
             raise ValueError("The GPU codebook has no decode table.")
@@ -161,54 +173,53 @@ class TileDecoder:
 
     def prepare_batch(self, groups):
         """Builds the device descriptors of one launch over DeviceGroups of
-        one dtype (neuralzip/gpu/decoder.py:130-191)."""
+        any mix of dtypes (neuralzip/gpu/decoder.py:130-191)."""
         groups = tuple(groups)
         if not groups:
             raise ValueError("A decode batch must contain at least one group.")
         device = groups[0].output.device
         if device.type != "cuda" or any(g.output.device != device for g in groups):
             raise ValueError("A decode batch must use one CUDA device.")
-        spec = groups[0].spec
-        if any(g.spec != spec for g in groups):
-            raise ValueError("A decode batch must use one layout.")
+        layouts = [_layout_of(g.spec) for g in groups]
+        if any(code is None for code in layouts):
+            raise ValueError("The GPU decoder has no kernel for this dtype layout.")
         table = np.zeros(len(groups), dtype=_native.GROUP_DTYPE)
         for g in groups:
             if g.lut_index != _native.RAW_LUT and (g.bits % 16 or g.lut_ptr % 16):
                 raise ValueError("Bitstreams and decode tables must be 16-byte aligned.")
         for i, g in enumerate(groups):
             table[i] = (g.bits, g.lens, g.tile_off, g.lanes, g.out, g.numel, g.lut_index)
-        # Works sorted by decode table so each CTA stages one table.
-        lut_ids = sorted({g.lut_index for g in groups})
+        lut_ids = sorted({g.lut_index for g in groups if g.lut_index != _native.RAW_LUT})
         lut_slot = {lut: i for i, lut in enumerate(lut_ids)}
         lut_ptrs = np.array([next(g.lut_ptr for g in groups if g.lut_index == lut) for lut in lut_ids],
                             dtype=np.uint64)
         lut_words = {g.lut_index: g.lut_words for g in groups}
         for i, g in enumerate(groups):
             table[i]["lut"] = _native.RAW_LUT if g.lut_index == _native.RAW_LUT else lut_slot[g.lut_index]
-        order = sorted(range(len(groups)), key=lambda i: (groups[i].lut_index, i))
-        total_works = sum(groups[i].tiles for i in order)
-        lut_works = {lut: (sum(g.tiles for g in groups if g.lut_index == lut), lut == _native.RAW_LUT)
-                     for lut in lut_ids}
-        layout = (spec.element_size, bool(spec.bit_reorder), spec.mantissa_bits, spec.exponent_bits,
-                  spec.gpu_stream)
-        nw, per_cta = self.staging_policy(device.index, lut_works, layout)
+        # Works sorted by (layout, decode table): each CTA stages one table
+        # and runs one layout.
+        keys = sorted({(layouts[i], g.lut_index) for i, g in enumerate(groups)})
+        members = {key: [i for i, g in enumerate(groups) if (layouts[i], g.lut_index) == key] for key in keys}
+        key_works = {key: (sum(groups[i].tiles for i in members[key]), key[0], key[1] == _native.RAW_LUT)
+                     for key in keys}
+        total_works = sum(n for n, _, _ in key_works.values())
+        nw, per_cta = self.staging_policy(device.index, key_works)
         works = np.zeros(total_works, dtype=_native.WORK_DTYPE)
         ctas = []
         cursor = 0
-        for lut in lut_ids:
+        for key in keys:
+            layout, lut = key
             begin = cursor
-            for i in order:
-                if groups[i].lut_index != lut:
-                    continue
+            for i in members[key]:
                 n = groups[i].tiles
                 works["group"][cursor:cursor + n] = i
                 works["tile"][cursor:cursor + n] = np.arange(n, dtype=np.uint32)
                 cursor += n
             slot = _native.RAW_LUT if lut == _native.RAW_LUT else lut_slot[lut]
             words = 0 if lut == _native.RAW_LUT else lut_words[lut]
-            step = max(1, int(per_cta[lut]))
+            step = max(1, int(per_cta[key]))
             for start in range(begin, cursor, step):
-                ctas.append((slot, start, min(cursor, start + step), words))
+                ctas.append((slot, start, min(cursor, start + step), words, layout))
         cta_array = np.array(ctas, dtype=_native.CTA_DTYPE)
         if not len(lut_ptrs):
             lut_ptrs = np.zeros(1, dtype=np.uint64)
@@ -218,13 +229,12 @@ class TileDecoder:
         )
         status = torch.zeros(1, dtype=torch.int32, device=device)
         launch = _native.Launch()
-        launch.dtype = _native_dtype(spec)
         launch.warps_per_cta = nw
         launch.groups, launch.works, launch.ctas, launch.luts = (t.data_ptr() for t in tensors)
         launch.status = status.data_ptr()
         launch.n_ctas = len(cta_array)
         return PreparedBatch(
-            descriptor_tensors=tensors, device=device, layout=layout, warps_per_cta=nw,
+            descriptor_tensors=tensors, device=device, layout=tuple(sorted(set(layouts))), warps_per_cta=nw,
             shared_memory=shared_memory_bytes(nw), kernel_grid=(len(cta_array),), launch=launch,
             outputs=tuple(g.output for g in groups), status=status, works=total_works,
             elements=sum(g.numel for g in groups),

@@ -642,11 +642,21 @@ class NeuralZipRuntime:
         torch.cuda.synchronize(self.device)
 
     def _prepare(self, items):
-        """One prepared launch per dtype over `items` (uploaded groups)."""
-        per_dtype = defaultdict(list)
+        """Prepared launches over `items` (uploaded groups of any dtypes):
+        one for the dtype with the most elements and, if there are others,
+        one more launch that mixes all of them. The big launch runs alone
+        and fills every SM; small dtypes are latency-bound and decode faster
+        in a launch of their own geometry than as extra CTAs of the big one
+        (the reference keeps one launch per layout)."""
+        by_dtype = defaultdict(list)
         for item in items:
-            per_dtype[item.group.encoded.dtype.name].append(item.device)
-        return tuple(self._decoder.prepare_batch(batch) for batch in per_dtype.values())
+            by_dtype[item.group.encoded.dtype.torch_dtype].append(item.device)
+        main = max(by_dtype, key=lambda dtype: sum(d.numel for d in by_dtype[dtype]))
+        rest = [d for dtype, devices in by_dtype.items() if dtype != main for d in devices]
+        batches = [self._decoder.prepare_batch(by_dtype[main])]
+        if rest:
+            batches.append(self._decoder.prepare_batch(rest))
+        return tuple(batches)
 
     @classmethod
     def attach(cls, model, exported, *, device=None, overlap=True, prefetch_depth=2, blocks_per_launch="auto"):

@@ -205,12 +205,11 @@ def test_c_abi_launch_by_hand():
     groups = np.zeros(1, dtype=_native.GROUP_DTYPE)
     groups[0] = (dg.bits, dg.lens, dg.tile_off, dg.lanes, dg.out, numel, 0)
     works = np.array([(0, t) for t in range(dg.tiles)], dtype=_native.WORK_DTYPE)
-    ctas = np.array([(0, 0, dg.tiles, dg.lut_words)], dtype=_native.CTA_DTYPE)
+    ctas = np.array([(0, 0, dg.tiles, dg.lut_words, _native.LAYOUT_FP32)], dtype=_native.CTA_DTYPE)
     luts = np.array([dg.lut_ptr], dtype=np.uint64)
     dev = [torch.from_numpy(a.view(np.uint8).copy()).cuda() for a in (groups, works, ctas, luts)]
     status = torch.zeros(1, dtype=torch.int32, device="cuda")
     launch = _native.Launch()
-    launch.dtype = _native.dtype_struct(4, 1, 23, 8, 3)
     launch.warps_per_cta = 4
     launch.groups, launch.works, launch.ctas, launch.luts = (t.data_ptr() for t in dev)
     launch.status = status.data_ptr()
@@ -219,11 +218,18 @@ def test_c_abi_launch_by_hand():
     torch.cuda.synchronize()
     assert bytes(out.cpu().view(torch.uint8).numpy()) == raw
     assert int(status.item()) == 0
+    # A CTA that names no known layout writes nothing and reports status 3.
+    out.view(torch.int32).fill_(-1)
+    ctas["layout"] = 7
+    dev[2].copy_(torch.from_numpy(ctas.view(np.uint8).copy()))
+    _native.decode_launch(launch, torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 3
+    assert bool((out.view(torch.int32) == -1).all())
 
 
 def test_launch_rejects_bad_geometry():
     launch = _native.Launch()
-    launch.dtype = _native.dtype_struct(2, 1, 7, 8, 1)
     launch.warps_per_cta = 5
     launch.n_ctas = 1
     launch.groups = launch.works = launch.ctas = launch.luts = 1
@@ -253,6 +259,38 @@ def test_tiny_and_ragged_groups(dtype):
         groups.append(_device_group(raw, spec, book, out, arena, lut_index=i))
         expected.append(raw)
     prepared = decoder.prepare_batch(groups)
+    decoder.decode_batch(prepared)
+    torch.cuda.synchronize()
+    for g, raw in zip(groups, expected):
+        assert bytes(g.output.cpu().view(torch.uint8).numpy()) == raw
+    decoder.check_status(prepared)
+
+
+def test_one_launch_mixes_layouts():
+    """bf16, fp16 and fp32 groups (singleton, mixed and raw) in one batch:
+    one launch, each CTA runs its own layout."""
+    decoder = gpu_decoder.default_decoder()
+    arena, groups, expected = [], [], []
+    index = 0
+    for dtype in (torch.bfloat16, torch.float16, torch.float32):
+        spec = DTYPES[dtype]
+        for numel, sigma in ((3 * 8192 + 11, 0.02), (131072, 1.0)):
+            raw = H.gaussian_raw(numel, sigma, dtype, 60 + index)
+            sel = H.selected_lane(raw, spec)
+            if spec.exponent_stream is not None and sigma > 0.5:
+                lengths, vocab = H.mixed_book_for(sel)
+                book = GPUCodebook(tuple(lengths), tuple(int(v) for v in O.mixed_codes(lengths)), vocab)
+            else:
+                header, _ = _native.huff0_build(np.bincount(sel, minlength=256) + 1, 12)
+                lengths, values, _, _ = _native.huff0_read(header)
+                book = GPUCodebook(tuple(lengths), values)
+            out = torch.full((numel,), -1, dtype=torch.int16 if spec.element_size == 2 else torch.int32,
+                             device="cuda").view(dtype)
+            groups.append(_device_group(raw, spec, book, out, arena, lut_index=index))
+            expected.append(raw)
+            index += 1
+    prepared = decoder.prepare_batch(groups)
+    assert prepared.layout == (_native.LAYOUT_BF16, _native.LAYOUT_FP16, _native.LAYOUT_FP32)
     decoder.decode_batch(prepared)
     torch.cuda.synchronize()
     for g, raw in zip(groups, expected):

@@ -296,3 +296,20 @@ def test_one_launch_mixes_layouts():
     for g, raw in zip(groups, expected):
         assert bytes(g.output.cpu().view(torch.uint8).numpy()) == raw
     decoder.check_status(prepared)
+
+
+def test_config1_single_tensor_singleton():
+    """BASELINE config 1 on the GPU: 128 singleton-coded chunks of one
+    4096x4096 bf16 tensor decode bit-exactly through the runtime."""
+    from neuralzip_b200.gpu.inference import NeuralZipRuntime, export_tensors_for_gpu
+    from neuralzip_b200.setup import NeuralZipSetup
+
+    g = torch.Generator().manual_seed(0)
+    named = {"w": (torch.randn(4096, 4096, generator=g) * 0.02).to(torch.bfloat16)}
+    setup = NeuralZipSetup(chunk_size=256 << 10, cluster_js_threshold=0.05, enable_packed_codebooks=False).build(named)
+    export = export_tensors_for_gpu(named, setup)
+    runtime = NeuralZipRuntime(None, export, "cuda:0")
+    runtime.workspaces[torch.bfloat16].view(torch.uint8).fill_(0xA5)
+    got = dict(runtime.materialized_weights())["w"]
+    assert torch.equal(got.view(torch.uint8), named["w"].reshape(-1).view(torch.uint8))
+    runtime.check_status()

@@ -154,3 +154,30 @@ def test_hf_wrapper_ordinary_load_and_compressed_reload():
             if source == original_path:
                 restored.save_pretrained(compressed_path)
                 assert restored.neuralzip_stats.representation == "storage"
+
+
+@pytest.mark.gpu
+def test_tied_embedding_qwen2_logits_bitwise():
+    """Config 3's architecture family (Qwen2, tied embeddings): the tied
+    lm_head/embedding stays resident, every other linear weight is decoded
+    per block, and logits equal the uncompressed model's bit for bit."""
+    from transformers import Qwen2Config, Qwen2ForCausalLM
+
+    config = Qwen2Config(vocab_size=128, hidden_size=128, intermediate_size=352, num_hidden_layers=2,
+                         num_attention_heads=4, num_key_value_heads=2, tie_word_embeddings=True)
+    config._attn_implementation = "eager"
+    torch.manual_seed(0)
+    model = Qwen2ForCausalLM(config).bfloat16().eval().cuda()
+    tokens = torch.arange(24, device="cuda").reshape(1, -1)
+    with torch.no_grad():
+        expected = model(tokens, use_cache=False).logits.clone()
+    setup = neuralzip.setup(model, chunk_size=8192)
+    exported = export_model_for_gpu(model, setup)
+    names = {b.tensor_name for b in exported.bindings}
+    assert "lm_head.weight" not in names and "model.embed_tokens.weight" not in names
+    runtime = NeuralZipRuntime.attach(model, exported, device="cuda:0")
+    for workspace in runtime.workspaces.values():
+        workspace.view(torch.uint8).fill_(0xA5)
+    with torch.no_grad():
+        assert exact(model(tokens, use_cache=False).logits, expected)
+    runtime.check_status()

@@ -201,3 +201,23 @@ def test_multithreaded_pack_matches_single_chunk():
         assert bytes(enc.symbols.bitstream) == bytes(one.symbols.bitstream)
         assert bytes(enc.symbols.lane_bits) == bytes(one.symbols.lane_bits)
         assert enc.symbols.tile_offsets == one.symbols.tile_offsets
+
+
+def test_config1_storage_round_trip():
+    """BASELINE config 1 on the CPU path: a 4096x4096 bf16 N(0, 0.02) tensor
+    (seed 0), 256 KiB chunks, JS threshold 0.05, singleton (Huff0) codes
+    only; storage v2 encode and decode are bit-exact and the export packs
+    every chunk with a singleton table."""
+    g = torch.Generator().manual_seed(0)
+    named = {"w": (torch.randn(4096, 4096, generator=g) * 0.02).to(torch.bfloat16)}
+    setup = NeuralZipSetup(chunk_size=256 << 10, cluster_js_threshold=0.05,
+                           enable_packed_codebooks=False).build(named)
+    assert setup.codebooks and all(b.mode == "shared_huff0" for b in setup.codebooks)
+    blob, metadata, sizes, _ = NeuralZipCompressor(setup, threads=4).encode(named.items())
+    assert sizes["compressed_bytes"] < sizes["raw_bytes"]
+    decoded = NeuralZipCompressor().decode(blob, metadata)
+    assert torch.equal(decoded["w"].view(torch.uint8), named["w"].view(torch.uint8))
+    from neuralzip_b200.gpu.inference import export_tensors_for_gpu
+
+    export = export_tensors_for_gpu(named, setup)
+    assert len(export.groups) == 128 and all(not g.codebook.vocab and g.codebook.max_bits for g in export.groups)

@@ -311,5 +311,5 @@ def test_config1_single_tensor_singleton():
     runtime = NeuralZipRuntime(None, export, "cuda:0")
     runtime.workspaces[torch.bfloat16].view(torch.uint8).fill_(0xA5)
     got = dict(runtime.materialized_weights())["w"]
-    assert torch.equal(got.view(torch.uint8), named["w"].reshape(-1).view(torch.uint8))
+    assert torch.equal(got.reshape(-1).view(torch.uint8), named["w"].reshape(-1).view(torch.uint8))
     runtime.check_status()

@@ -426,11 +426,15 @@ def main():
 
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
+    # Ranks share the host: each builds its workload on its share of the cores.
+    host_threads = max(1, (os.cpu_count() or 1) // world)
+    if world > 1:
+        torch.set_num_threads(host_threads)
     t0 = time.perf_counter()
     named = config2(1 + rank, args.bf16_tensors)
     setup = NeuralZipSetup().build(named)
     t_setup = time.perf_counter() - t0
-    export = export_tensors_for_gpu(named, setup)
+    export = export_tensors_for_gpu(named, setup, threads=host_threads)
     t_export = time.perf_counter() - t0 - t_setup
     runtime = NeuralZipRuntime(None, export, device)
     block = export.block_order[0]
@@ -563,6 +567,7 @@ def main():
                 "codebooks": sorted({(b.mode, len(b.vocab) // 2) for b in setup.codebooks}),
                 "l2": "inputs and outputs larger than L2 (no flush)", "setup_s": round(t_setup, 1),
                 "export_s": round(t_export, 1), "parallelism": f"{world} independent ranks",
+                "host_cores": os.cpu_count(),
             },
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind, "traffic": traffic,

@@ -68,13 +68,13 @@ __device__ __forceinline__ void stg_u4(void* p, uint32_t a, uint32_t b, uint32_t
 
 // MSB-first window over 32-bit words (bit 31 earliest). The valid bits are
 // the top `avail` bits of hi:lo and everything below them is zero. The next
-// word is requested one refill ahead (pf); a deeper queue of registers does
-// not help, since moving a pending load's register waits for the load. All
-// shifts are 32-bit funnel shifts.
+// word is requested one refill ahead (pf). The refill stays a branch: a
+// form without one (selects, or moves of the words through registers on
+// every lookup) reads pf on every lookup and so waits for its load there.
+// All shifts are 32-bit funnel shifts.
 struct Window {
     uint32_t hi, lo, avail, pf;
-    const uint32_t* src;  // next word to request
-
+    const uint32_t* src;
     __device__ __forceinline__ void init(const uint32_t* words, uint32_t bitpos) {
         const uint32_t* p = words + (bitpos >> 5);
         const uint32_t sh = bitpos & 31U;
@@ -85,7 +85,7 @@ struct Window {
         lo = w1 << sh;
         avail = 64U - sh;
     }
-    // Drops n (< 32) bits; only the low five bits of n are used.
+    // Drops n & 31 bits (a table entry's code length is its low five bits).
     __device__ __forceinline__ void consume(uint32_t n) {
         hi = __funnelshift_l(lo, hi, n);
         lo = __funnelshift_l(0U, lo, n);
@@ -104,12 +104,12 @@ struct Window {
 
 // Code longer than 12 bits: consume the 12-bit prefix, then walk the suffix
 // tree one bit at a time (at most 44 steps). Returns a leaf word (byte
-// count in bits 5..7, bytes in 8..23, zero shift). A table that exceeds the
-// depth sets *status and yields one zero byte, so the lane still finishes.
+// count in bits 5..7, bytes in 8..23). A table that exceeds the depth sets
+// *status and yields one zero byte, so the lane still finishes.
 __device__ __forceinline__ uint32_t walk_long(const uint32_t* __restrict__ table, uint32_t marker, Window& w,
                                               int32_t* status) {
     w.consume(NZ_LUT_BITS);
-    uint32_t node = (marker >> 8) & kTreeMask;
+    uint32_t node = (marker >> 16) & kTreeMask;
     uint32_t leaf = 0;
     for (uint32_t d = 0; d < kMaxTreeDepth; ++d) {
         w.top_up();
@@ -117,7 +117,7 @@ __device__ __forceinline__ uint32_t walk_long(const uint32_t* __restrict__ table
         w.consume(1);
         const uint32_t child = table[NZ_LUT_TREE + 2U * node + bit];
         if (child & 0xE0U) {
-            leaf = child & ~0x1FU;
+            leaf = child;
             break;
         }
         node = (child >> 8) & kTreeMask;
@@ -129,8 +129,15 @@ __device__ __forceinline__ uint32_t walk_long(const uint32_t* __restrict__ table
     return leaf;
 }
 
+// Bitwise select: bits of a where m is set, bits of b elsewhere (one LOP3).
+__device__ __forceinline__ uint32_t bsel(uint32_t a, uint32_t b, uint32_t m) { return (a & m) | (b & ~m); }
+
 // Element assembly (undoes DTypeSpec.reorder_bytes, neuralzip/dtypes.py:
-// 23-45; the reference kernel's assemble_value, decode.cu:83-100).
+// 23-45; the reference kernel's assemble_value, decode.cu:83-100). The
+// reorder is undone on four elements at once, byte-wise: for bf16 the raw
+// byte is sign|mant7 and the decoded byte the exponent, so the element's
+// high byte is sign|exp[7:1] and its low byte exp[0]|mant7; fp32 does the
+// same on its third byte.
 template <int ES, bool REORDER>
 struct Layout;
 
@@ -139,16 +146,18 @@ template <bool REORDER>
 struct Layout<2, REORDER> {
     static constexpr int kSel = 1;
     static constexpr int kRawLanes = 1;
-    __device__ __forceinline__ static uint32_t pair(uint32_t r, uint32_t x, uint32_t sel) {
-        const uint32_t t = __byte_perm(r, x, sel);
-        if (!REORDER) return t;
-        return (t & 0x007F007FU) | ((t >> 1) & 0x7F807F80U) | ((t << 8) & 0x80008000U);
-    }
     // 8 elements from raw bytes r[0] (lane 0) and decoded bytes x0, x1.
     __device__ __forceinline__ static void store8(uint8_t* out, uint32_t e, const uint2* r, uint32_t x0,
                                                   uint32_t x1) {
-        stg_u4(out + 2ull * e, pair(r[0].x, x0, 0x5140), pair(r[0].x, x0, 0x7362), pair(r[0].y, x1, 0x5140),
-               pair(r[0].y, x1, 0x7362));
+        uint32_t l0 = r[0].x, h0 = x0, l1 = r[0].y, h1 = x1;
+        if (REORDER) {
+            h0 = bsel(r[0].x, x0 >> 1, 0x80808080U);
+            l0 = bsel(r[0].x, x0 << 7, 0x7F7F7F7FU);
+            h1 = bsel(r[0].y, x1 >> 1, 0x80808080U);
+            l1 = bsel(r[0].y, x1 << 7, 0x7F7F7F7FU);
+        }
+        stg_u4(out + 2ull * e, __byte_perm(l0, h0, 0x5140), __byte_perm(l0, h0, 0x7362),
+               __byte_perm(l1, h1, 0x5140), __byte_perm(l1, h1, 0x7362));
     }
     __device__ __forceinline__ static void store1(uint8_t* out, const uint8_t* const* lanes, uint32_t e,
                                                   uint32_t x) {
@@ -163,28 +172,28 @@ template <>
 struct Layout<4, true> {
     static constexpr int kSel = 3;
     static constexpr int kRawLanes = 3;
-    __device__ __forceinline__ static uint32_t fix(uint32_t v) {
-        return (v & 0x007FFFFFU) | ((v >> 1) & 0x7F800000U) | ((v << 8) & 0x80000000U);
-    }
-    __device__ __forceinline__ static uint32_t word(uint32_t l0, uint32_t l1, uint32_t l2, uint32_t x,
-                                                    uint32_t i) {
-        const uint32_t lo = __byte_perm(l0, l1, i | ((i + 4U) << 4));
-        const uint32_t hi = __byte_perm(l2, x, i | ((i + 4U) << 4));
-        return fix(__byte_perm(lo, hi, 0x5410));
+    // Four elements from byte lanes a, b (raw), c (raw sign|mant[22:16]) and
+    // x (exponents): undo the reorder on c/x, then a 4x4 byte transpose.
+    __device__ __forceinline__ static void store4(uint8_t* o, uint32_t a, uint32_t b, uint32_t c, uint32_t x) {
+        const uint32_t hi = bsel(c, x >> 1, 0x80808080U);
+        const uint32_t mid = bsel(c, x << 7, 0x7F7F7F7FU);
+        const uint32_t t0 = __byte_perm(a, b, 0x5140), t1 = __byte_perm(a, b, 0x7362);
+        const uint32_t t2 = __byte_perm(mid, hi, 0x5140), t3 = __byte_perm(mid, hi, 0x7362);
+        stg_u4(o, __byte_perm(t0, t2, 0x5410), __byte_perm(t0, t2, 0x7632), __byte_perm(t1, t3, 0x5410),
+               __byte_perm(t1, t3, 0x7632));
     }
     __device__ __forceinline__ static void store8(uint8_t* out, uint32_t e, const uint2* r, uint32_t x0,
                                                   uint32_t x1) {
         uint8_t* o = out + 4ull * e;
-        stg_u4(o, word(r[0].x, r[1].x, r[2].x, x0, 0), word(r[0].x, r[1].x, r[2].x, x0, 1),
-               word(r[0].x, r[1].x, r[2].x, x0, 2), word(r[0].x, r[1].x, r[2].x, x0, 3));
-        stg_u4(o + 16, word(r[0].y, r[1].y, r[2].y, x1, 0), word(r[0].y, r[1].y, r[2].y, x1, 1),
-               word(r[0].y, r[1].y, r[2].y, x1, 2), word(r[0].y, r[1].y, r[2].y, x1, 3));
+        store4(o, r[0].x, r[1].x, r[2].x, x0);
+        store4(o + 16, r[0].y, r[1].y, r[2].y, x1);
     }
     __device__ __forceinline__ static void store1(uint8_t* out, const uint8_t* const* lanes, uint32_t e,
                                                   uint32_t x) {
         const uint32_t v = static_cast<uint32_t>(lanes[0][e]) | (static_cast<uint32_t>(lanes[1][e]) << 8) |
                            (static_cast<uint32_t>(lanes[2][e]) << 16) | (x << 24);
-        reinterpret_cast<uint32_t*>(out)[e] = fix(v);
+        reinterpret_cast<uint32_t*>(out)[e] =
+            (v & 0x007FFFFFU) | ((v >> 1) & 0x7F800000U) | ((v << 8) & 0x80000000U);
     }
 };
 
@@ -199,6 +208,35 @@ __device__ __forceinline__ void merge_tail(uint8_t* out, const uint8_t* const* l
     }
 }
 
+// Raw-lane bytes of one merge group: kGroup passes of 8 elements per lane.
+template <int ES, bool REORDER>
+struct MergeGroup {
+    static constexpr uint32_t kGroup = ES == 4 ? 2 : 4;
+    uint2 raw[kGroup][Layout<ES, REORDER>::kRawLanes];
+
+    // Loads group g of a staging round; every element is inside the group
+    // and every lane 16-byte aligned (interior tiles only).
+    __device__ __forceinline__ void load(const uint8_t* const* lanes, uint32_t base, uint32_t g, uint32_t lane) {
+#pragma unroll
+        for (uint32_t k = 0; k < kGroup; ++k) {
+            const uint32_t rrow = (g * kGroup + k) * kRowsPerPass + lane / kLanesPerRow;
+            const uint32_t ex = base + rrow * NZ_LANE_ELEMS + (lane % kLanesPerRow) * 8U;
+#pragma unroll
+            for (int l = 0; l < Layout<ES, REORDER>::kRawLanes; ++l) raw[k][l] = ldg_u2(lanes[l] + ex);
+        }
+    }
+    __device__ __forceinline__ void store(uint8_t* out, const uint32_t* stage, uint32_t base, uint32_t g,
+                                          uint32_t lane) const {
+#pragma unroll
+        for (uint32_t k = 0; k < kGroup; ++k) {
+            const uint32_t rrow = (g * kGroup + k) * kRowsPerPass + lane / kLanesPerRow;
+            const uint32_t col = (lane % kLanesPerRow) * 8U;
+            const uint32_t* src = stage + rrow * kStageStride + (col >> 2);
+            Layout<ES, REORDER>::store8(out, base + rrow * NZ_LANE_ELEMS + col, raw[k], src[0], src[1]);
+        }
+    }
+};
+
 // The works [begin, end) of one CTA, taken in turn by its NW warps, for
 // one element layout. `table` is the CTA's staged decode table.
 template <int ES, bool REORDER, int NW>
@@ -207,8 +245,11 @@ __device__ __forceinline__ void decode_works(const nz_group* __restrict__ groups
                                              uint32_t end, const uint32_t* __restrict__ table,
                                              uint32_t* stage, int32_t* __restrict__ status) {
     using L = Layout<ES, REORDER>;
+    using G = MergeGroup<ES, REORDER>;
+    constexpr uint32_t kGroups = kMergePasses / G::kGroup;
     const uint32_t warp = threadIdx.x >> 5;
     const uint32_t lane = threadIdx.x & 31U;
+    const uint2* table2 = reinterpret_cast<const uint2*>(table);
     for (uint32_t w = begin + warp; w < end; w += NW) {
         const nz_work item = works[w];
         const nz_group& g = groups[item.group];
@@ -254,6 +295,10 @@ __device__ __forceinline__ void decode_works(const nz_group* __restrict__ groups
         const uint32_t s = item.tile * NZ_TILE_LANES + lane;
         const uint32_t first = s * NZ_LANE_ELEMS;
         const uint32_t n_lane = first < numel ? min(NZ_LANE_ELEMS, numel - first) : 0U;
+        // Every element of an interior tile is inside the group and every
+        // lane 16-byte aligned: its merges need no bounds checks, and each
+        // round's first raw loads are issued before the round's decode.
+        const bool interior = vec_ok && tile_base + NZ_TILE_ELEMS <= numel;
         const uint32_t len = reinterpret_cast<const uint16_t*>(g.lens)[s];
         uint32_t incl = len;
 #pragma unroll
@@ -266,10 +311,10 @@ __device__ __forceinline__ void decode_works(const nz_group* __restrict__ groups
         // 16-byte bounds, which stay inside the stream and its zero pad; a
         // raw lane's ragged end (< 16 bytes) is left to the loads.
         const uint32_t tile_bits = __shfl_sync(0xFFFFFFFFU, incl, 31);
+        const uint32_t bit0 = reinterpret_cast<const uint32_t*>(g.tile_off)[item.tile];
         if (lane == 0) {
-            const uint32_t b0 = reinterpret_cast<const uint32_t*>(g.tile_off)[item.tile];
-            const uint32_t w0 = (b0 >> 5) & ~3U;
-            const uint32_t w1 = ((b0 + tile_bits + 127U) >> 7) << 2;
+            const uint32_t w0 = (bit0 >> 5) & ~3U;
+            const uint32_t w1 = ((bit0 + tile_bits + 127U) >> 7) << 2;
             prefetch_l2(reinterpret_cast<const uint32_t*>(g.bits) + w0, (w1 - w0) * 4U);
             if (vec_ok) {
                 const uint32_t n = min(NZ_TILE_ELEMS, numel - tile_base);
@@ -278,64 +323,82 @@ __device__ __forceinline__ void decode_works(const nz_group* __restrict__ groups
             }
         }
         Window win;
-        win.init(reinterpret_cast<const uint32_t*>(g.bits),
-                 reinterpret_cast<const uint32_t*>(g.tile_off)[item.tile] + incl - len);
-        // Byte queue qb:qa, `qbits` bits queued (<= 24 between iterations,
-        // <= 56 after a 4-byte push, so one flush per lookup suffices).
-        uint32_t qa = 0, qb = 0, qbits = 0;
+        win.init(reinterpret_cast<const uint32_t*>(g.bits), bit0 + incl - len);
+        // Byte queue: `qbits` bits (0, 8, 16 or 24) of decoded bytes wait in
+        // qa between lookups. A lookup's bytes that do not fit in qa are not
+        // kept: when qa fills up it is stored and rebuilt from the entry.
+        uint32_t qa = 0, qbits = 0;
         uint32_t* row = stage + lane * kStageStride;
 
         for (uint32_t r = 0; r < kRounds; ++r) {
             const uint32_t done = r * kRoundElems;
             if (__all_sync(0xFFFFFFFFU, n_lane <= done)) break;
+            const uint32_t base = tile_base + done;
+            // bf16/fp16 keep two groups of raw bytes in flight; fp32 (three
+            // raw lanes) loads each group just before it merges, within the
+            // 64-register budget.
+            constexpr bool kAhead = ES == 2;
+            G raw[2];
+            if (kAhead && interior) raw[0].load(lanes, base, 0, lane);
             const uint32_t want = n_lane > done ? min(kRoundElems, n_lane - done) : 0U;
             const uint32_t target = (want + 3U) >> 2;
             for (uint32_t wi = 0; wi < target;) {
-                const uint2 entry = reinterpret_cast<const uint2*>(table)[win.hi >> (32 - NZ_LUT_BITS)];
+                const uint2 entry = table2[win.hi >> (32 - NZ_LUT_BITS)];
                 uint32_t e = entry.x, x = entry.y;
-                if ((e & 0xE0U) == 0U) {
-                    e = walk_long(table, e, win, status);
-                    x = e >> 8;
+                if ((e & 0xFF00U) == 0U) {
+                    const uint32_t leaf = walk_long(table, e, win, status);
+                    e = ((leaf >> 5) & 7U) << 11;
+                    x = leaf >> 8;
                 }
                 win.consume(e);
                 win.top_up();
                 qa |= x << qbits;
-                qb |= __funnelshift_l(x, 0U, qbits);
-                qbits += (e >> 2) & 0x38U;
-                if (qbits >= 32U) {
+                const uint32_t qn = qbits + (e >> 8);  // < 64
+                if (qn >= 32U) {
                     row[wi++] = qa;
-                    qa = qb;
-                    qb = 0;
-                    qbits -= 32U;
+                    qa = __funnelshift_l(x, 0U, qbits);
                 }
+                qbits = qn & 31U;
             }
             __syncwarp();
-            // Merge the 32 staged rows: kLanesPerRow lanes per row, 8
-            // elements per lane; loads of a group of passes are issued first.
-            const uint32_t col = (lane % kLanesPerRow) * 8U;
-            constexpr uint32_t kGroup = ES == 4 ? 2 : 4;
+            if (interior) {
+                // Merge the 32 staged rows, kLanesPerRow lanes per row and 8
+                // elements per lane; each group's raw loads are in flight
+                // while the previous group merges.
 #pragma unroll
-            for (uint32_t p0 = 0; p0 < kMergePasses; p0 += kGroup) {
-                uint2 raw[kGroup][L::kRawLanes];
-                uint32_t ex[kGroup];
-                bool full[kGroup];
-#pragma unroll
-                for (uint32_t k = 0; k < kGroup; ++k) {
-                    const uint32_t rrow = (p0 + k) * kRowsPerPass + lane / kLanesPerRow;
-                    ex[k] = tile_base + rrow * NZ_LANE_ELEMS + done + col;
-                    full[k] = vec_ok && ex[k] + 8U <= numel;
-                    if (full[k]) {
-#pragma unroll
-                        for (int l = 0; l < L::kRawLanes; ++l) raw[k][l] = ldg_u2(lanes[l] + ex[k]);
+                for (uint32_t gi = 0; gi < kGroups; ++gi) {
+                    if (kAhead) {
+                        if (gi + 1 < kGroups) raw[(gi + 1) & 1U].load(lanes, base, gi + 1, lane);
+                    } else {
+                        raw[0].load(lanes, base, gi, lane);
                     }
+                    raw[kAhead ? (gi & 1U) : 0U].store(out, stage, base, gi, lane);
                 }
+            } else {
+                const uint32_t col = (lane % kLanesPerRow) * 8U;
 #pragma unroll
-                for (uint32_t k = 0; k < kGroup; ++k) {
-                    const uint32_t rrow = (p0 + k) * kRowsPerPass + lane / kLanesPerRow;
-                    const uint32_t* src = stage + rrow * kStageStride + (col >> 2);
-                    const uint32_t x0 = src[0], x1 = src[1];
-                    if (full[k]) L::store8(out, ex[k], raw[k], x0, x1);
-                    else if (ex[k] < numel) merge_tail<ES, REORDER>(out, lanes, ex[k], numel, x0, x1);
+                for (uint32_t p0 = 0; p0 < kMergePasses; p0 += G::kGroup) {
+                    uint2 raw[G::kGroup][L::kRawLanes];
+                    uint32_t ex[G::kGroup];
+                    bool full[G::kGroup];
+#pragma unroll
+                    for (uint32_t k = 0; k < G::kGroup; ++k) {
+                        const uint32_t rrow = (p0 + k) * kRowsPerPass + lane / kLanesPerRow;
+                        ex[k] = base + rrow * NZ_LANE_ELEMS + col;
+                        full[k] = vec_ok && ex[k] + 8U <= numel;
+                        if (full[k]) {
+#pragma unroll
+                            for (int l = 0; l < L::kRawLanes; ++l) raw[k][l] = ldg_u2(lanes[l] + ex[k]);
+                        }
+                    }
+#pragma unroll
+                    for (uint32_t k = 0; k < G::kGroup; ++k) {
+                        const uint32_t rrow = (p0 + k) * kRowsPerPass + lane / kLanesPerRow;
+                        const uint32_t* src = stage + rrow * kStageStride + (col >> 2);
+                        const uint32_t x0 = src[0], x1 = src[1];
+                        if (full[k]) L::store8(out, ex[k], raw[k], x0, x1);
+                        else if (ex[k] < numel) merge_tail<ES, REORDER>(out, lanes, ex[k], numel, x0, x1);
+                    }
                 }
             }
             __syncwarp();

@@ -119,16 +119,18 @@ std::vector<uint64_t> canonical_mixed_codes(const uint8_t* lengths, uint32_t nsy
 
 // Multi-symbol decode table: NZ_LUT_ENTRIES entries of two words, then the
 // suffix tree. Entry for a 12-bit window (word 0 / word 1):
-//   w0 bits 0..3  window bits the decoded tokens consume (1..12); bit 4 is
-//                 zero so the low five bits are directly a shift amount
-//   w0 bits 5..7  number of decoded bytes (1..4)
-//   w1            up to four decoded bytes (first byte lowest)
-// A window whose first code is longer than 12 bits instead has a zero byte
-// count and the index of the trie node reached after 12 bits in w0 bits
-// 8..31; the kernel then walks the suffix tree at word NZ_LUT_TREE, two
-// words per node (child for bit 0, child for bit 1): a child with a nonzero
-// byte count (bits 5..7) is a leaf with its bytes in bits 8..23, any other
-// child holds the next node index in bits 8..31.
+//   w0 bits 0..4   window bits the decoded tokens consume (1..12)
+//   w0 bits 5..7   zero: the kernel adds w0 to its bit offset, and only
+//                  carries out of bits 0..4 may reach bit 5
+//   w0 bits 8..15  eight times the number of decoded bytes (8..32), the
+//                  amount the kernel's byte queue grows by
+//   w1             up to four decoded bytes (first byte lowest)
+// A window whose first code is longer than 12 bits instead has zero in
+// bits 0..15 and the index of the trie node reached after 12 bits in w0
+// bits 16..31; the kernel then walks the suffix tree at word NZ_LUT_TREE,
+// two words per node (child for bit 0, child for bit 1): a child with a
+// nonzero byte count (bits 5..7) is a leaf with its bytes in bits 8..23,
+// any other child holds the next node index in bits 8..31.
 void Codebook::build_lut() {
     std::vector<TrieNode> trie(1);
     for (uint32_t s = 0; s < nsym; ++s) {
@@ -217,7 +219,7 @@ void Codebook::build_lut() {
                     throw Error(NZ_EVALUE, "The Huffman codebook does not cover every prefix.");
             }
             if (trie[node].symbol < 0) {
-                if (pos == 0) meta = static_cast<uint32_t>(trie[node].suffix) << 8;
+                if (pos == 0) meta = static_cast<uint32_t>(trie[node].suffix) << 16;
                 break;
             }
             uint32_t value = 0;
@@ -227,7 +229,7 @@ void Codebook::build_lut() {
             nbytes += count;
             pos += depth;
         }
-        if (nbytes) meta = pos | (nbytes << 5);
+        if (nbytes) meta = pos | ((8U * nbytes) << 8);
         lut[2 * prefix] = meta;
         lut[2 * prefix + 1] = bytes;
     }

@@ -3,8 +3,10 @@
 Test helper: it runs the same per-lane algorithm as nz_tile_decode in
 neuralzip_b200/csrc/nz_decode.cu over the decode table produced by the
 product (nz_codebook_lut): 12-bit lookups of two-word entries (metadata
-whose low five bits are the shift amount, and up to four bytes), the suffix-tree walk for codes longer than 12
-bits, a byte queue flushed as 32-bit words, 128-element staging rounds, and
+with the code length in bits 0..4 and eight times the byte count in bits
+8..15, and up to four bytes), the suffix-tree
+walk for codes longer than 12 bits, a one-word byte queue whose overflow is
+rebuilt from the entry when a word is stored, 128-element staging rounds, and
 only the staged prefix of the table (rounded up to 16 bytes) visible, so
 table, staging and loop errors show up on a CPU. Expected bytes always come
 from the oracle, never from this model.
@@ -65,7 +67,7 @@ def decode_group(lut, bits, lens, tile_off, numel, lut_words=None):
             first = (tile * LANES + lane) * LANE
             n_lane = min(LANE, numel - first) if first < numel else 0
             win = _Window(bits, int(tile_off[tile]) + sum(lens_t[:lane]))
-            queue, qbits = 0, 0
+            qa, qbits = 0, 0
             for r in range(LANE // ROUND):
                 done = r * ROUND
                 want = min(ROUND, n_lane - done) if n_lane > done else 0
@@ -74,29 +76,58 @@ def decode_group(lut, bits, lens, tile_off, numel, lut_words=None):
                 while len(staged) < 4 * target:
                     k = win.buf >> 52
                     e, x = int(table[2 * k]), int(table[2 * k + 1])
-                    if (e & 0xE0) == 0:
+                    if (e & 0xFF00) == 0:
                         win.consume(12)
-                        node = (e >> 8) & 511
+                        node = (e >> 16) & 511
                         for _ in range(44):
                             win.top_up()
                             bit = win.buf >> 63
                             win.consume(1)
                             child = int(table[LUT_TREE + 2 * node + bit])
                             if child & 0xE0:
-                                e = child & ~0x1F
-                                x = e >> 8
+                                e = ((child >> 5) & 7) << 11
+                                x = child >> 8
                                 break
                             node = (child >> 8) & 511
                         else:
                             raise AssertionError("suffix walk exceeded 44 steps")
                     win.consume(e)
                     win.top_up()
-                    queue |= x << qbits
-                    qbits += ((e >> 5) & 7) * 8
-                    if qbits >= 32:
-                        staged += (queue & 0xFFFFFFFF).to_bytes(4, "little")
-                        queue >>= 32
-                        qbits -= 32
+                    qa = (qa | (x << qbits)) & 0xFFFFFFFF
+                    qn = qbits + (e >> 8)
+                    assert qn < 64, "entry byte count out of range"
+                    if qn >= 32:
+                        staged += qa.to_bytes(4, "little")
+                        qa = (x >> (32 - qbits)) if qbits else 0
+                    qbits = qn & 31
                 if want:
                     out[first + done:first + done + want] = np.frombuffer(bytes(staged), dtype=np.uint8)[:want]
     return out
+
+
+def byte_perm(a, b, sel):
+    """__byte_perm: byte i of the result is byte (sel >> 4i) & 7 of b:a."""
+    src = (int(b) << 32) | int(a)
+    return sum(((src >> (8 * ((sel >> (4 * i)) & 7))) & 0xFF) << (8 * i) for i in range(4))
+
+
+def bsel(a, b, m):
+    return (a & m) | (b & ~m & 0xFFFFFFFF)
+
+
+def merge_bf16_words(raw, exp):
+    """Two output words (4 bf16 elements) from 4 raw bytes (sign|mant7) and
+    4 decoded exponent bytes, as the kernel's store8 forms them."""
+    hi = bsel(raw, exp >> 1, 0x80808080)
+    lo = bsel(raw, (exp << 7) & 0xFFFFFFFF, 0x7F7F7F7F)
+    return byte_perm(lo, hi, 0x5140), byte_perm(lo, hi, 0x7362)
+
+
+def merge_fp32_words(a, b, c, exp):
+    """Four fp32 words from raw lanes a, b, c and decoded exponents (store4)."""
+    hi = bsel(c, exp >> 1, 0x80808080)
+    mid = bsel(c, (exp << 7) & 0xFFFFFFFF, 0x7F7F7F7F)
+    t0, t1 = byte_perm(a, b, 0x5140), byte_perm(a, b, 0x7362)
+    t2, t3 = byte_perm(mid, hi, 0x5140), byte_perm(mid, hi, 0x7362)
+    return (byte_perm(t0, t2, 0x5410), byte_perm(t0, t2, 0x7632), byte_perm(t1, t3, 0x5410),
+            byte_perm(t1, t3, 0x7632))

@@ -100,3 +100,28 @@ def test_empty_and_tiny_groups():
         _roundtrip(H.lanes_with(np.full(n, 127, dtype=np.uint8), spec), spec, book)
     enc = encode_with_codebook(b"", book, dtype=spec, stream_id=1)
     assert enc.numel == 0 and enc.symbols.bit_length == 0
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_merge_arithmetic_model_restores_elements(dtype):
+    """The kernel's byte-wise undo of the sign/exponent reorder (four
+    elements per step: bit selects, shifts and byte permutes) rebuilds the
+    original elements from the oracle's lane split."""
+    spec = DTYPES[dtype]
+    es = spec.element_size
+    rng = np.random.default_rng(7)
+    raw = rng.integers(0, 256, size=4 * es * 256, dtype=np.uint8)
+    raw[:4 * es * 4] = 0xFF  # all-ones and all-zero words
+    raw[4 * es * 4:4 * es * 8] = 0
+    lanes = O.split(raw, spec)
+
+    def word(lane, i):
+        return int.from_bytes(lanes[lane][4 * i:4 * i + 4].tobytes(), "little")
+
+    for i in range(256):
+        if es == 2:
+            words = KM.merge_bf16_words(word(0, i), word(1, i))
+        else:
+            words = KM.merge_fp32_words(word(0, i), word(1, i), word(2, i), word(3, i))
+        got = b"".join(w.to_bytes(4, "little") for w in words)
+        assert got == raw[4 * es * i:4 * es * (i + 1)].tobytes(), i

@@ -40,7 +40,14 @@ extern "C" {
 #define NZ_LUT_BITS 12u
 #define NZ_LUT_ENTRIES (1u << NZ_LUT_BITS)
 #define NZ_TREE_MAX_NODES 512u
-#define NZ_LUT_TREE (2u * NZ_LUT_ENTRIES)
+/* Decode-table layout (words): NZ_LUT_ENTRIES two-word entries, the
+ * canonical long-code tables (limits, rank offsets, tokens) at
+ * NZ_LUT_CANON, then the binary suffix tree at NZ_LUT_TREE. */
+#define NZ_LUT_CANON (2u * NZ_LUT_ENTRIES)
+#define NZ_CANON_MAX_BITS 31u
+#define NZ_CANON_TOKENS 512u
+#define NZ_CANON_WORDS (64u + NZ_CANON_TOKENS)
+#define NZ_LUT_TREE (NZ_LUT_CANON + NZ_CANON_WORDS)
 #define NZ_LUT_WORDS (NZ_LUT_TREE + 2u * NZ_TREE_MAX_NODES)
 #define NZ_MAX_CODE_BITS 56u
 #define NZ_MAX_SINGLETON_BITS 12u
@@ -99,6 +106,10 @@ int nz_codebook_info(const nz_codebook* codebook, uint32_t* longest,
  * neuralzip/gpu/inference.py:28-75). Writes NZ_LUT_WORDS words. */
 int nz_codebook_lut(const nz_codebook* codebook, uint32_t* lut,
                     uint32_t cap_words);
+/* Leading words of that table the kernel reads (and stages): the entries,
+ * plus the long-code tables when some code is longer than 12 bits. Part of
+ * GPUCodebook.decode_lut's size (neuralzip/gpu/inference.py:52-72). */
+int nz_codebook_table_words(const nz_codebook* codebook, uint32_t* words);
 
 /* Setup-time singleton tables (replaces build_codebook_from_counts ->
  * HUF_buildCTable_wksp + HUF_writeCTable_wksp, neuralzip/native/
@@ -234,7 +245,8 @@ typedef struct nz_cta {
  * nonzero code if a corrupt table made a lane give up (2) or a CTA named an
  * unknown layout (3); it is only written on error. Asynchronous on
  * `cuda_stream` (a cudaStream_t, NULL = legacy default stream).
- * warps_per_cta: 4, 8 or 16 (0 = default, 8). */
+ * warps_per_cta: 4, 8, 16 or 24 (0 = default, 8); 24-warp CTAs fill an SM
+ * alone, 8- and 4-warp CTAs run two and three to an SM. */
 typedef struct nz_launch {
     uint32_t warps_per_cta;
     uint32_t n_ctas;

@@ -25,7 +25,9 @@ TILE_ELEMS = LANE_ELEMS * TILE_LANES
 LUT_BITS = 12
 LUT_ENTRIES = 1 << LUT_BITS
 TREE_MAX_NODES = 512
-LUT_TREE = 2 * LUT_ENTRIES
+LUT_CANON = 2 * LUT_ENTRIES
+CANON_WORDS = 64 + 512
+LUT_TREE = LUT_CANON + CANON_WORDS
 LUT_WORDS = LUT_TREE + 2 * TREE_MAX_NODES
 MAX_CODE_BITS = 56
 BITS_PAD_WORDS = 16
@@ -74,7 +76,7 @@ assert GROUP_DTYPE.itemsize == 72 and WORK_DTYPE.itemsize == 8 and CTA_DTYPE.ite
 
 EXPORTS = (
     "nz_export_code_table", "nz_codebook_create", "nz_codebook_destroy", "nz_codebook_info",
-    "nz_codebook_lut", "nz_huff0_build", "nz_huff0_read", "nz_pack_bound", "nz_pack_chunk",
+    "nz_codebook_lut", "nz_codebook_table_words", "nz_huff0_build", "nz_huff0_read", "nz_pack_bound", "nz_pack_chunk",
     "nz_pack_many", "nz_split_lanes", "nz_exponent_histograms", "nz_count_tokens", "nz_mixed_encode", "nz_mixed_decode",
     "nz_huff0_encode", "nz_huff0_decode", "nz_decode_launch", "nz_decode_launch_many", "nz_decode_occupancy", "nz_decode_smem_bytes",
     "nz_schedule_create", "nz_schedule_destroy", "nz_schedule_enter", "nz_schedule_decode_unit",
@@ -118,6 +120,7 @@ def _declare(lib):
         "nz_codebook_destroy": [c.c_void_p],
         "nz_codebook_info": [c.c_void_p, u32p, u32p],
         "nz_codebook_lut": [c.c_void_p, c.c_void_p, c.c_uint32],
+        "nz_codebook_table_words": [c.c_void_p, u32p],
         "nz_huff0_build": [c.c_void_p, c.c_uint32, c.c_void_p, c.c_size_t, sizep, c.c_void_p],
         "nz_huff0_read": [c.c_void_p, c.c_size_t, c.c_void_p, c.c_void_p, u32p, sizep],
         "nz_pack_bound": [c.c_uint64, c.c_uint32, u64p, u64p, u64p],
@@ -206,6 +209,9 @@ class NativeCodebook:
         check(lib.nz_codebook_info(handle, ctypes.byref(longest), ctypes.byref(nodes)))
         self.longest = longest.value
         self.tree_nodes = nodes.value
+        words = ctypes.c_uint32()
+        check(lib.nz_codebook_table_words(handle, ctypes.byref(words)))
+        self.table_words = words.value
 
     def lut(self):
         out = np.zeros(LUT_WORDS, dtype=np.uint32)

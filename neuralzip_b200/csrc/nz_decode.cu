@@ -37,6 +37,15 @@ constexpr uint32_t kRoundElems = 128;                      // per lane per stagi
 constexpr uint32_t kRounds = NZ_LANE_ELEMS / kRoundElems;  // 2
 constexpr uint32_t kStageStride = kRoundElems / 4 + 1;     // words per staged row (odd: no conflicts)
 constexpr uint32_t kStageWordsPerWarp = NZ_TILE_LANES * kStageStride;
+// Widest CTA: one per SM, its shared memory (227 KB opt-in) split into the
+// decode table and, per warp, the staging rows plus a copy of the warp's
+// current tile bitstream (kBitBufWords, a multiple of four words).
+constexpr uint32_t kMaxWarps = 24;
+constexpr uint32_t kSmemPerBlock = 232448;
+constexpr uint32_t kBitBufWords =
+    ((kSmemPerBlock / 4U - NZ_LUT_WORDS) / kMaxWarps - kStageWordsPerWarp) & ~3U;
+constexpr uint32_t kWarpWords = kStageWordsPerWarp + kBitBufWords;
+static_assert((NZ_LUT_WORDS + kMaxWarps * kWarpWords) * 4U <= kSmemPerBlock, "shared memory of the widest CTA");
 constexpr uint32_t kLanesPerRow = kRoundElems / 8;          // merge: 8 elements per lane
 constexpr uint32_t kRowsPerPass = 32 / kLanesPerRow;
 constexpr uint32_t kMergePasses = NZ_TILE_LANES / kRowsPerPass;
@@ -68,18 +77,22 @@ __device__ __forceinline__ void stg_u4(void* p, uint32_t a, uint32_t b, uint32_t
 
 // MSB-first window over 32-bit words (bit 31 earliest). The valid bits are
 // the top `avail` bits of hi:lo and everything below them is zero. The next
-// word is requested one refill ahead (pf). The refill stays a branch: a
-// form without one (selects, or moves of the words through registers on
-// every lookup) reads pf on every lookup and so waits for its load there.
-// All shifts are 32-bit funnel shifts.
+// word is requested one refill ahead (pf). The words come from the warp's
+// shared-memory copy of its tile, or from global memory for a tile larger
+// than that copy (a generic pointer serves both): lanes refill at different
+// lookups, and a load's register is tracked for the whole warp, so a refill
+// waits for the loads other lanes issued just before; from shared memory
+// that wait is short. The refill stays a branch: a form without one reads
+// pf on every lookup and so waits for its load there. All shifts are
+// 32-bit funnel shifts.
 struct Window {
     uint32_t hi, lo, avail, pf;
     const uint32_t* src;
     __device__ __forceinline__ void init(const uint32_t* words, uint32_t bitpos) {
         const uint32_t* p = words + (bitpos >> 5);
         const uint32_t sh = bitpos & 31U;
-        const uint32_t w0 = __ldg(p), w1 = __ldg(p + 1);
-        pf = __ldg(p + 2);
+        const uint32_t w0 = p[0], w1 = p[1];
+        pf = p[2];
         src = p + 3;
         hi = __funnelshift_l(w1, w0, sh);
         lo = w1 << sh;
@@ -97,7 +110,7 @@ struct Window {
             hi |= __funnelshift_rc(pf, 0U, avail);
             lo = __funnelshift_rc(0U, pf, avail);
             avail += 32U;
-            pf = __ldg(src++);
+            pf = *src++;
         }
     }
 };
@@ -123,6 +136,31 @@ __device__ __forceinline__ uint32_t walk_long(const uint32_t* __restrict__ table
         node = (child >> 8) & kTreeMask;
     }
     if (!leaf) {
+        if (status) *status = kStatusCorruptTable;
+        leaf = 1U << 5;
+    }
+    return leaf;
+}
+
+// Code longer than 12 bits (the entry has no bytes). With canonical
+// long-code tables (marker bit 31 clear) the code's length is the first one,
+// from the shortest under this 12-bit prefix up, whose limit the 32-bit
+// window does not exceed, and its rank in code order is the window's top L
+// bits plus that length's offset: a couple of shared-memory reads instead
+// of one tree step per bit. Otherwise the suffix tree is walked. Returns a
+// leaf word; a table that does not resolve the window sets *status and
+// yields one zero byte.
+__device__ __forceinline__ uint32_t decode_long(const uint32_t* __restrict__ table, uint32_t marker, Window& w,
+                                                int32_t* status) {
+    if (marker & 0x80000000U) return walk_long(table, marker, w, status);
+    const uint32_t* canon = table + NZ_LUT_CANON;
+    const uint32_t win = w.hi;  // at least 33 valid bits: the whole code
+    uint32_t len = max((marker >> 16) & 31U, NZ_LUT_BITS + 1U);
+    while (win > canon[len] && len < NZ_CANON_MAX_BITS) ++len;
+    const uint32_t rank = canon[32U + len] + (win >> (32U - len));
+    uint32_t leaf = canon[64U + min(rank, NZ_CANON_TOKENS - 1U)];
+    w.consume(len);
+    if (win > canon[len] || (leaf & 0xE0U) == 0U) {
         if (status) *status = kStatusCorruptTable;
         leaf = 1U << 5;
     }
@@ -322,8 +360,33 @@ __device__ __forceinline__ void decode_works(const nz_group* __restrict__ groups
                 for (int l = 0; l < L::kRawLanes; ++l) prefetch_l2(lanes[l] + tile_base, n);
             }
         }
+        // The tile's bits, from the 16-byte word boundary at or below its
+        // first bit through four words past its last one (the read-ahead),
+        // are copied into the warp's buffer when they fit; inside the stream
+        // and its 16-word zero pad.
         Window win;
-        win.init(reinterpret_cast<const uint32_t*>(g.bits), bit0 + incl - len);
+        {
+            const uint32_t* gbits = reinterpret_cast<const uint32_t*>(g.bits);
+            const uint32_t wa = (bit0 >> 5) & ~3U;
+            const uint32_t wb = (((bit0 + tile_bits) >> 5) + 8U) & ~3U;
+            if (wb - wa <= kBitBufWords) {
+                uint32_t* buf = stage + kStageWordsPerWarp;
+                const uint32_t sbuf = static_cast<uint32_t>(__cvta_generic_to_shared(buf));
+#pragma unroll
+                for (uint32_t k = 0; k < (kBitBufWords + 127U) / 128U; ++k) {
+                    const uint32_t i = lane * 4U + k * 128U;
+                    if (i < wb - wa)
+                        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(sbuf + 4U * i),
+                                     "l"(gbits + wa + i)
+                                     : "memory");
+                }
+                asm volatile("cp.async.wait_all;" ::: "memory");
+                __syncwarp();
+                win.init(buf - wa, bit0 + incl - len);
+            } else {
+                win.init(gbits, bit0 + incl - len);
+            }
+        }
         // Byte queue: `qbits` bits (0, 8, 16 or 24) of decoded bytes wait in
         // qa between lookups. A lookup's bytes that do not fit in qa are not
         // kept: when qa fills up it is stored and rebuilt from the entry.
@@ -346,7 +409,7 @@ __device__ __forceinline__ void decode_works(const nz_group* __restrict__ groups
                 const uint2 entry = table2[win.hi >> (32 - NZ_LUT_BITS)];
                 uint32_t e = entry.x, x = entry.y;
                 if ((e & 0xFF00U) == 0U) {
-                    const uint32_t leaf = walk_long(table, e, win, status);
+                    const uint32_t leaf = decode_long(table, e, win, status);
                     e = ((leaf >> 5) & 7U) << 11;
                     x = leaf >> 8;
                 }
@@ -412,13 +475,13 @@ constexpr int32_t kStatusBadLayout = 3;
 // decode table and runs the body of its layout (uniform per CTA, so the
 // switch does not diverge).
 template <int NW>
-__global__ void __launch_bounds__(NW * 32, (NW >= 16 ? 2 : (NW >= 8 ? 4 : 8)))
+__global__ void __launch_bounds__(NW * 32, (NW >= 16 ? 1 : (NW >= 8 ? 2 : 3)))
     nz_tile_decode(const nz_group* __restrict__ groups, const nz_work* __restrict__ works,
                    const nz_cta* __restrict__ ctas, const uint64_t* __restrict__ luts,
                    int32_t* __restrict__ status) {
     extern __shared__ __align__(16) uint32_t smem[];
     uint32_t* table = smem;
-    uint32_t* stage = smem + NZ_LUT_WORDS + (threadIdx.x >> 5) * kStageWordsPerWarp;
+    uint32_t* stage = smem + NZ_LUT_WORDS + (threadIdx.x >> 5) * kWarpWords;
 
     const nz_cta cta = ctas[blockIdx.x];
     if (cta.lut != NZ_RAW_LUT) {
@@ -445,7 +508,7 @@ __global__ void __launch_bounds__(NW * 32, (NW >= 16 ? 2 : (NW >= 8 ? 4 : 8)))
 
 template <int NW>
 constexpr size_t smem_bytes() {
-    return (NZ_LUT_WORDS + NW * kStageWordsPerWarp) * sizeof(uint32_t);
+    return (NZ_LUT_WORDS + NW * kWarpWords) * sizeof(uint32_t);
 }
 
 // Opts the instantiation into its dynamic shared memory (once per process).
@@ -475,6 +538,7 @@ cudaError_t launch_nw(const nz_launch& l, cudaStream_t stream) {
     switch (l.warps_per_cta) {
         case 4: return launch_one<4>(l, stream);
         case 16: return launch_one<16>(l, stream);
+        case 24: return launch_one<24>(l, stream);
         default: return launch_one<8>(l, stream);
     }
 }
@@ -533,7 +597,7 @@ extern "C" {
 int nz_decode_smem_bytes(uint32_t warps_per_cta, uint32_t* bytes) {
     if (!bytes) return nz::fail(NZ_EVALUE, "Null output.");
     const uint32_t nw = warps_per_cta == 0 ? 8U : warps_per_cta;
-    *bytes = (NZ_LUT_WORDS + nw * kStageWordsPerWarp) * static_cast<uint32_t>(sizeof(uint32_t));
+    *bytes = (NZ_LUT_WORDS + nw * kWarpWords) * static_cast<uint32_t>(sizeof(uint32_t));
     return NZ_OK;
 }
 
@@ -546,7 +610,8 @@ int nz_decode_occupancy(uint32_t warps_per_cta, uint32_t* ctas_per_sm) {
         case 0:
         case 8: err = occupancy_one<8>(&ctas); break;
         case 16: err = occupancy_one<16>(&ctas); break;
-        default: return nz::fail(NZ_EVALUE, "warps_per_cta must be 4, 8 or 16.");
+        case 24: err = occupancy_one<24>(&ctas); break;
+        default: return nz::fail(NZ_EVALUE, "warps_per_cta must be 4, 8, 16 or 24.");
     }
     if (err != cudaSuccess)
         return nz::fail(NZ_ECUDA, std::string("CUDA occupancy query failed: ") + cudaGetErrorString(err));
@@ -598,8 +663,8 @@ int nz_decode_launch(const nz_launch* launch, void* cuda_stream) {
     if (!l.groups || !l.works || !l.ctas || !l.luts)
         return nz::fail(NZ_EVALUE, "Null device descriptor array.");
     if (l.warps_per_cta != 0 && l.warps_per_cta != 4 && l.warps_per_cta != 8 &&
-        l.warps_per_cta != 16)
-        return nz::fail(NZ_EVALUE, "warps_per_cta must be 4, 8 or 16.");
+        l.warps_per_cta != 16 && l.warps_per_cta != 24)
+        return nz::fail(NZ_EVALUE, "warps_per_cta must be 4, 8, 16 or 24.");
     const cudaError_t err = launch_nw(l, reinterpret_cast<cudaStream_t>(cuda_stream));
     if (err != cudaSuccess)
         return nz::fail(NZ_ECUDA, std::string("CUDA launch failed: ") + cudaGetErrorString(err));

@@ -118,19 +118,28 @@ std::vector<uint64_t> canonical_mixed_codes(const uint8_t* lengths, uint32_t nsy
 }
 
 // Multi-symbol decode table: NZ_LUT_ENTRIES entries of two words, then the
-// suffix tree. Entry for a 12-bit window (word 0 / word 1):
+// canonical long-code tables, then the suffix tree. Entry for a 12-bit
+// window (word 0 / word 1):
 //   w0 bits 0..4   window bits the decoded tokens consume (1..12)
-//   w0 bits 5..7   zero: the kernel adds w0 to its bit offset, and only
-//                  carries out of bits 0..4 may reach bit 5
+//   w0 bits 5..7   zero
 //   w0 bits 8..15  eight times the number of decoded bytes (8..32), the
 //                  amount the kernel's byte queue grows by
 //   w1             up to four decoded bytes (first byte lowest)
 // A window whose first code is longer than 12 bits instead has zero in
-// bits 0..15 and the index of the trie node reached after 12 bits in w0
-// bits 16..31; the kernel then walks the suffix tree at word NZ_LUT_TREE,
-// two words per node (child for bit 0, child for bit 1): a child with a
-// nonzero byte count (bits 5..7) is a leaf with its bytes in bits 8..23,
-// any other child holds the next node index in bits 8..31.
+// bits 0..15 of w0, and in bits 16..31 either
+//   * the shortest code length under that 12-bit prefix (bit 31 clear):
+//     the code is then found by comparing the 32-bit window with the
+//     canonical limits at NZ_LUT_CANON (words 0..31: the largest
+//     left-justified window of each length, words 32..63: rank offset of
+//     each length, words 64..: the leaf word of each long code in code
+//     order); used when every long code is at most 31 bits and the long
+//     codes are numbered in canonical order (consecutive values per length,
+//     lengths growing with the value); or
+//   * bit 31 set and the index of the trie node reached after 12 bits in
+//     bits 16..30: the kernel walks the suffix tree at word NZ_LUT_TREE,
+//     two words per node (child for bit 0, child for bit 1).
+// A leaf word has its byte count in bits 5..7 and its bytes in bits 8..23;
+// any other tree child holds the next node index in bits 8..31.
 void Codebook::build_lut() {
     std::vector<TrieNode> trie(1);
     for (uint32_t s = 0; s < nsym; ++s) {
@@ -205,6 +214,41 @@ void Codebook::build_lut() {
     }
 
     lut.assign(NZ_LUT_WORDS, 0);
+    // Canonical long-code tables: codes longer than 12 bits, in the order of
+    // their left-justified values.
+    std::vector<uint32_t> long_syms;
+    for (uint32_t s = 0; s < nsym; ++s)
+        if (lengths[s] > NZ_LUT_BITS) long_syms.push_back(s);
+    auto left = [&](uint32_t s) { return codes[s] << (64 - lengths[s]); };
+    std::sort(long_syms.begin(), long_syms.end(), [&](uint32_t a, uint32_t b) { return left(a) < left(b); });
+    bool canonical = !long_syms.empty() && longest <= NZ_CANON_MAX_BITS && long_syms.size() <= NZ_CANON_TOKENS;
+    for (size_t i = 1; canonical && i < long_syms.size(); ++i) {
+        const uint32_t a = long_syms[i - 1], b = long_syms[i];
+        if (lengths[b] < lengths[a] || (lengths[b] == lengths[a] && codes[b] != codes[a] + 1)) canonical = false;
+    }
+    std::vector<uint32_t> shortest_under(NZ_LUT_ENTRIES, 0);
+    if (canonical) {
+        uint32_t* limit = lut.data() + NZ_LUT_CANON;
+        uint32_t* offset = limit + 32;
+        uint32_t* token = limit + 64;
+        // limit[L]: the largest 32-bit window decoded by a code of length <= L
+        // (the next code's left-justified start minus one).
+        for (uint32_t L = 0; L < 32; ++L) limit[L] = 0xFFFFFFFFU;
+        for (size_t i = 0; i < long_syms.size(); ++i) {
+            const uint32_t s = long_syms[i], L = lengths[s];
+            const uint32_t prefix = static_cast<uint32_t>(codes[s] >> (L - NZ_LUT_BITS));
+            if (!shortest_under[prefix] || L < shortest_under[prefix]) shortest_under[prefix] = L;
+            if (i == 0 || lengths[long_syms[i - 1]] != L)
+                offset[L] = static_cast<uint32_t>(i) - static_cast<uint32_t>(codes[s]);
+            if (i + 1 < long_syms.size() && lengths[long_syms[i + 1]] != L) {
+                const uint32_t next_start = static_cast<uint32_t>(left(long_syms[i + 1]) >> 32);
+                for (uint32_t k = L; k < lengths[long_syms[i + 1]]; ++k) limit[k] = next_start - 1U;
+            }
+            uint32_t value = 0;
+            const uint32_t count = token_bytes(static_cast<int>(s), &value);
+            token[i] = (value << 8) | (count << 5);
+        }
+    }
     for (uint32_t prefix = 0; prefix < NZ_LUT_ENTRIES; ++prefix) {
         uint32_t pos = 0, nbytes = 0, bytes = 0;
         uint32_t meta = 0;
@@ -219,7 +263,9 @@ void Codebook::build_lut() {
                     throw Error(NZ_EVALUE, "The Huffman codebook does not cover every prefix.");
             }
             if (trie[node].symbol < 0) {
-                if (pos == 0) meta = static_cast<uint32_t>(trie[node].suffix) << 16;
+                if (pos == 0)
+                    meta = canonical ? shortest_under[prefix] << 16
+                                     : 0x80000000U | (static_cast<uint32_t>(trie[node].suffix) << 16);
                 break;
             }
             uint32_t value = 0;
@@ -254,6 +300,9 @@ void Codebook::build_lut() {
             lut[NZ_LUT_TREE + 2 * static_cast<uint32_t>(node.suffix) + b] = word;
         }
     }
+    table_words = long_syms.empty() ? NZ_LUT_CANON
+                  : canonical       ? NZ_LUT_TREE
+                                    : NZ_LUT_TREE + 2 * tree_nodes;
 }
 
 // ---------------------------------------------------------------------------
@@ -487,6 +536,13 @@ int nz_codebook_info(const nz_codebook* codebook, uint32_t* longest, uint32_t* t
         const auto* cb = reinterpret_cast<const nz::Codebook*>(codebook);
         if (longest) *longest = cb->longest;
         if (tree_nodes) *tree_nodes = cb->tree_nodes;
+    })
+}
+
+int nz_codebook_table_words(const nz_codebook* codebook, uint32_t* words) {
+    NZ_GUARD({
+        if (!codebook || !words) throw Error(NZ_EVALUE, "Null codebook argument.");
+        *words = reinterpret_cast<const nz::Codebook*>(codebook)->table_words;
     })
 }
 

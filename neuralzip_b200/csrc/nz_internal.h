@@ -25,6 +25,7 @@ struct Codebook {
     uint32_t nsym = 0;
     uint32_t longest = 0;
     uint32_t tree_nodes = 0;
+    uint32_t table_words = 0;  // leading lut words the kernel reads
     std::vector<uint8_t> lengths;
     std::vector<uint64_t> codes;
     std::vector<uint16_t> vocab;        // pair k -> first | second << 8

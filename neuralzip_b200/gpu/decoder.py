@@ -30,7 +30,11 @@ import torch
 from neuralzip_b200 import _native
 
 KERNEL_PATH = Path(__file__).resolve().parent.parent / "csrc" / "nz_decode.cu"
-WARPS_PER_CTA = 16
+WARPS_PER_CTA = 24
+# CTA widths the launch plan picks from, widest first (the kernel's
+# instantiations: 24-warp CTAs fill an SM alone, 8- and 4-warp CTAs run two
+# and three to an SM).
+CTA_WIDTHS = (24, 8, 4)
 SM_COUNT_DEFAULT = 148
 # Cost of a coded tile relative to a pair-coded bf16 tile (measured on
 # config 2: fp16 bytes are singleton-coded, fewer bytes per lookup; fp32
@@ -111,15 +115,13 @@ class TileDecoder:
         smallest count whose CTAs fit in one wave of resident CTAs: a launch
         then ends when its busiest warps do, instead of with a partial last
         wave that leaves SMs idle. A launch with fewer tiles than one
-        16-warp CTA per SM uses narrower CTAs so that every SM gets work
-        (16-warp CTAs hold the most resident warps: 32 per SM against 24
-        and 16 for 8- and 4-warp CTAs, whose shared memory is mostly the
-        36 KB table)."""
+        24-warp CTA per SM uses narrower CTAs so that every SM gets work
+        (a 24-warp CTA fills an SM's shared memory with the 38 KB table and
+        each warp's staging rows and tile-bitstream copy; 8- and 4-warp CTAs
+        run two and three to an SM, 16 and 12 warps)."""
         sms = self._sms(device_index)
         total = sum(n for n, _, _ in key_works.values())
-        nw = WARPS_PER_CTA
-        while nw > 4 and total < sms * nw:
-            nw //= 2
+        nw = next((w for w in CTA_WIDTHS if total >= sms * w), CTA_WIDTHS[-1])
         slots = self._occupancy(device_index, nw) * sms
 
         def per_warp_of(layout, raw):
@@ -141,10 +143,10 @@ class TileDecoder:
 
     def _occupancy(self, device_index, nw):
         """Resident CTAs per SM (CUDA occupancy calculator; shared memory
-        allows 2, 3 and 4 CTAs of 16, 8 and 4 warps on a B200)."""
+        allows 1, 1, 2 and 3 CTAs of 24, 16, 8 and 4 warps on a B200)."""
         key = (device_index, nw)
         if key not in self._ctas_per_sm:
-            fallback = {16: 2, 8: 3, 4: 4}[nw]
+            fallback = {24: 1, 16: 1, 8: 2, 4: 3}[nw]
             try:
                 with torch.cuda.device(device_index):
                     self._ctas_per_sm[key] = _native.decode_occupancy(nw) or fallback

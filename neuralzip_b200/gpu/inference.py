@@ -84,10 +84,11 @@ class GPUCodebook:
 
     @property
     def table_words(self):
-        """Words of the decode table the kernel stages (table + suffix tree)."""
+        """Words of the decode table the kernel stages (entries, plus the
+        long-code tables when a code is longer than 12 bits)."""
         if self.native is None:
             return 0
-        return (_native.LUT_TREE + 2 * self.native.tree_nodes + 3) // 4 * 4
+        return (self.native.table_words + 3) // 4 * 4
 
 
 @dataclass(frozen=True)

@@ -4,8 +4,8 @@ Test helper: it runs the same per-lane algorithm as nz_tile_decode in
 neuralzip_b200/csrc/nz_decode.cu over the decode table produced by the
 product (nz_codebook_lut): 12-bit lookups of two-word entries (metadata
 with the code length in bits 0..4 and eight times the byte count in bits
-8..15, and up to four bytes), the suffix-tree
-walk for codes longer than 12 bits, a one-word byte queue whose overflow is
+8..15, and up to four bytes), codes longer than 12 bits through the
+canonical limit/offset/leaf tables or the suffix-tree walk, a one-word byte queue whose overflow is
 rebuilt from the entry when a word is stored, 128-element staging rounds, and
 only the staged prefix of the table (rounded up to 16 bytes) visible, so
 table, staging and loop errors show up on a CPU. Expected bytes always come
@@ -17,7 +17,8 @@ import numpy as np
 LANE, LANES, TILE = 256, 32, 8192
 ROUND = 128
 LUT_ENTRIES = 4096
-LUT_TREE = 2 * LUT_ENTRIES
+LUT_CANON = 2 * LUT_ENTRIES
+LUT_TREE = LUT_CANON + 64 + 512
 MASK64 = (1 << 64) - 1
 
 
@@ -76,7 +77,7 @@ def decode_group(lut, bits, lens, tile_off, numel, lut_words=None):
                 while len(staged) < 4 * target:
                     k = win.buf >> 52
                     e, x = int(table[2 * k]), int(table[2 * k + 1])
-                    if (e & 0xFF00) == 0:
+                    if (e & 0xFF00) == 0 and e >> 31:
                         win.consume(12)
                         node = (e >> 16) & 511
                         for _ in range(44):
@@ -91,6 +92,20 @@ def decode_group(lut, bits, lens, tile_off, numel, lut_words=None):
                             node = (child >> 8) & 511
                         else:
                             raise AssertionError("suffix walk exceeded 44 steps")
+                    elif (e & 0xFF00) == 0:
+                        # canonical long code: limits, rank offsets, leaf words
+                        w32 = win.buf >> 32
+                        length = max((e >> 16) & 31, 13)
+                        while w32 > int(table[LUT_CANON + length]) and length < 31:
+                            length += 1
+                        assert w32 <= int(table[LUT_CANON + length]), "window beyond the last canonical limit"
+                        rank = (int(table[LUT_CANON + 32 + length]) + (w32 >> (32 - length))) & 0xFFFFFFFF
+                        assert rank < 512, "canonical rank out of range"
+                        leaf = int(table[LUT_CANON + 64 + rank])
+                        assert leaf & 0xE0, "empty canonical leaf"
+                        win.consume(length)
+                        e = ((leaf >> 5) & 7) << 11
+                        x = leaf >> 8
                     win.consume(e)
                     win.top_up()
                     qa = (qa | (x << qbits)) & 0xFFFFFFFF

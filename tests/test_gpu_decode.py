@@ -59,7 +59,7 @@ def single_group_model(raw, spec, book):
     return model, export, original
 
 
-@pytest.mark.parametrize("max_bits", [12, 32, 33, 56])
+@pytest.mark.parametrize("max_bits", [12, 13, 20, 31, 32, 33, 56])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
 def test_segment_boundaries(max_bits, dtype):
     spec = DTYPES[dtype]

@@ -39,11 +39,19 @@ def _roundtrip(raw, spec, book, model=True):
     return enc
 
 
-@pytest.mark.parametrize("max_bits", [12, 32, 33, 56])
+@pytest.mark.parametrize("max_bits", [12, 13, 20, 31, 32, 33, 56])
 def test_segment_books_roundtrip(max_bits):
     lengths = H.segment_lengths(max_bits)
     values = O.mixed_codes(lengths)
     book = GPUCodebook(tuple(lengths), tuple(int(v) for v in values), H.VOCAB)
+    # Codes of 13..31 bits decode through the canonical tables (the entries
+    # and those tables are staged); longer ones walk the suffix tree too.
+    if max_bits == 12:
+        assert book.table_words == _native.LUT_CANON
+    elif max_bits <= 31:
+        assert book.table_words == _native.LUT_TREE
+    else:
+        assert book.table_words > _native.LUT_TREE
     for spec in DTYPES.values():
         raw = H.lanes_with(H.segment_symbols(), spec)
         _roundtrip(raw, spec, book, model=spec.name == "bfloat16")

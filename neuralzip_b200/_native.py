@@ -79,6 +79,7 @@ EXPORTS = (
     "nz_codebook_lut", "nz_codebook_table_words", "nz_huff0_build", "nz_huff0_read", "nz_pack_bound", "nz_pack_chunk",
     "nz_pack_many", "nz_split_lanes", "nz_exponent_histograms", "nz_count_tokens", "nz_mixed_encode", "nz_mixed_decode",
     "nz_huff0_encode", "nz_huff0_decode", "nz_decode_launch", "nz_decode_launch_many", "nz_decode_occupancy", "nz_decode_smem_bytes",
+    "nz_decode_tile_words",
     "nz_schedule_create", "nz_schedule_destroy", "nz_schedule_enter", "nz_schedule_decode_unit",
     "nz_schedule_drain", "nz_schedule_mark", "nz_last_error",
     "nz_abi_version",
@@ -144,6 +145,7 @@ def _declare(lib):
         "nz_schedule_drain": [c.c_void_p, c.c_void_p],
         "nz_schedule_mark": [c.c_void_p, c.c_uint32, c.c_uint32],
         "nz_decode_smem_bytes": [c.c_uint32, u32p],
+        "nz_decode_tile_words": [c.c_uint32, u32p],
         "nz_last_error": [c.c_char_p, c.c_size_t],
         "nz_abi_version": [],
     }
@@ -377,6 +379,14 @@ def decode_smem_bytes(warps_per_cta=8):
     lib = load()
     out = ctypes.c_uint32()
     check(lib.nz_decode_smem_bytes(int(warps_per_cta), ctypes.byref(out)))
+    return out.value
+
+
+def decode_tile_words(warps_per_cta):
+    """Bitstream words of one tile a warp stages in shared memory."""
+    lib = load()
+    out = ctypes.c_uint32()
+    check(lib.nz_decode_tile_words(int(warps_per_cta), ctypes.byref(out)))
     return out.value
 
 

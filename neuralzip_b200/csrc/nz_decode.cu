@@ -37,15 +37,29 @@ constexpr uint32_t kRoundElems = 128;                      // per lane per stagi
 constexpr uint32_t kRounds = NZ_LANE_ELEMS / kRoundElems;  // 2
 constexpr uint32_t kStageStride = kRoundElems / 4 + 1;     // words per staged row (odd: no conflicts)
 constexpr uint32_t kStageWordsPerWarp = NZ_TILE_LANES * kStageStride;
-// Widest CTA: one per SM, its shared memory (227 KB opt-in) split into the
-// decode table and, per warp, the staging rows plus a copy of the warp's
-// current tile bitstream (kBitBufWords, a multiple of four words).
-constexpr uint32_t kMaxWarps = 24;
-constexpr uint32_t kSmemPerBlock = 232448;
-constexpr uint32_t kBitBufWords =
-    ((kSmemPerBlock / 4U - NZ_LUT_WORDS) / kMaxWarps - kStageWordsPerWarp) & ~3U;
-constexpr uint32_t kWarpWords = kStageWordsPerWarp + kBitBufWords;
-static_assert((NZ_LUT_WORDS + kMaxWarps * kWarpWords) * 4U <= kSmemPerBlock, "shared memory of the widest CTA");
+// A CTA's shared memory holds the decode table and, per warp, the staging
+// rows plus a copy of the warp's current tile bitstream. CTAs of 24 and 16
+// warps run one to an SM, of 8 and 4 warps two and three; each width gets
+// the largest bitstream copy (a multiple of four words) that keeps that
+// many CTAs resident: 956, 1964, 1336 and 1296 words.
+constexpr uint32_t kSmemPerSm = 233472;     // 228 KB
+constexpr uint32_t kSmemPerBlock = 232448;  // 227 KB opt-in limit
+constexpr uint32_t kSmemReserved = 1024;    // per resident CTA
+__host__ __device__ constexpr uint32_t ctas_per_sm(uint32_t nw) { return nw >= 16 ? 1U : (nw >= 8 ? 2U : 3U); }
+__host__ __device__ constexpr uint32_t bit_buf_words(uint32_t nw) {
+    return (((kSmemPerSm / ctas_per_sm(nw) - kSmemReserved < kSmemPerBlock
+                  ? kSmemPerSm / ctas_per_sm(nw) - kSmemReserved
+                  : kSmemPerBlock) /
+                 4U -
+             NZ_LUT_WORDS) /
+                nw -
+            kStageWordsPerWarp) &
+           ~3U;
+}
+__host__ __device__ constexpr uint32_t warp_words(uint32_t nw) { return kStageWordsPerWarp + bit_buf_words(nw); }
+static_assert(bit_buf_words(24) == 956 && bit_buf_words(16) == 1964 && bit_buf_words(8) == 1336 &&
+                  bit_buf_words(4) == 1296,
+              "bitstream copy per warp");
 constexpr uint32_t kLanesPerRow = kRoundElems / 8;          // merge: 8 elements per lane
 constexpr uint32_t kRowsPerPass = 32 / kLanesPerRow;
 constexpr uint32_t kMergePasses = NZ_TILE_LANES / kRowsPerPass;
@@ -282,6 +296,7 @@ __device__ __forceinline__ void decode_works(const nz_group* __restrict__ groups
                                              const nz_work* __restrict__ works, uint32_t begin,
                                              uint32_t end, const uint32_t* __restrict__ table,
                                              uint32_t* stage, int32_t* __restrict__ status) {
+    constexpr uint32_t kBitBufWords = bit_buf_words(NW);
     using L = Layout<ES, REORDER>;
     using G = MergeGroup<ES, REORDER>;
     constexpr uint32_t kGroups = kMergePasses / G::kGroup;
@@ -475,13 +490,13 @@ constexpr int32_t kStatusBadLayout = 3;
 // decode table and runs the body of its layout (uniform per CTA, so the
 // switch does not diverge).
 template <int NW>
-__global__ void __launch_bounds__(NW * 32, (NW >= 16 ? 1 : (NW >= 8 ? 2 : 3)))
+__global__ void __launch_bounds__(NW * 32, ctas_per_sm(NW))
     nz_tile_decode(const nz_group* __restrict__ groups, const nz_work* __restrict__ works,
                    const nz_cta* __restrict__ ctas, const uint64_t* __restrict__ luts,
                    int32_t* __restrict__ status) {
     extern __shared__ __align__(16) uint32_t smem[];
     uint32_t* table = smem;
-    uint32_t* stage = smem + NZ_LUT_WORDS + (threadIdx.x >> 5) * kWarpWords;
+    uint32_t* stage = smem + NZ_LUT_WORDS + (threadIdx.x >> 5) * warp_words(NW);
 
     const nz_cta cta = ctas[blockIdx.x];
     if (cta.lut != NZ_RAW_LUT) {
@@ -508,7 +523,7 @@ __global__ void __launch_bounds__(NW * 32, (NW >= 16 ? 1 : (NW >= 8 ? 2 : 3)))
 
 template <int NW>
 constexpr size_t smem_bytes() {
-    return (NZ_LUT_WORDS + NW * kWarpWords) * sizeof(uint32_t);
+    return (NZ_LUT_WORDS + NW * warp_words(NW)) * sizeof(uint32_t);
 }
 
 // Opts the instantiation into its dynamic shared memory (once per process).
@@ -597,7 +612,16 @@ extern "C" {
 int nz_decode_smem_bytes(uint32_t warps_per_cta, uint32_t* bytes) {
     if (!bytes) return nz::fail(NZ_EVALUE, "Null output.");
     const uint32_t nw = warps_per_cta == 0 ? 8U : warps_per_cta;
-    *bytes = (NZ_LUT_WORDS + nw * kWarpWords) * static_cast<uint32_t>(sizeof(uint32_t));
+    *bytes = (NZ_LUT_WORDS + nw * warp_words(nw)) * static_cast<uint32_t>(sizeof(uint32_t));
+    return NZ_OK;
+}
+
+int nz_decode_tile_words(uint32_t warps_per_cta, uint32_t* words) {
+    if (!words) return nz::fail(NZ_EVALUE, "Null output.");
+    const uint32_t nw = warps_per_cta == 0 ? 8U : warps_per_cta;
+    if (nw != 4 && nw != 8 && nw != 16 && nw != 24)
+        return nz::fail(NZ_EVALUE, "warps_per_cta must be 4, 8, 16 or 24.");
+    *words = bit_buf_words(nw);
     return NZ_OK;
 }
 

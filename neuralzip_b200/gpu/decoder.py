@@ -32,9 +32,10 @@ from neuralzip_b200 import _native
 KERNEL_PATH = Path(__file__).resolve().parent.parent / "csrc" / "nz_decode.cu"
 WARPS_PER_CTA = 24
 # CTA widths the launch plan picks from, widest first (the kernel's
-# instantiations: 24-warp CTAs fill an SM alone, 8- and 4-warp CTAs run two
-# and three to an SM).
-CTA_WIDTHS = (24, 8, 4)
+# instantiations: 24- and 16-warp CTAs fill an SM alone, 8- and 4-warp CTAs
+# run two and three to an SM; narrower ones give each warp a larger copy of
+# its tile's bitstream).
+CTA_WIDTHS = (24, 16, 8, 4)
 SM_COUNT_DEFAULT = 148
 # Cost of a coded tile relative to a pair-coded bf16 tile (measured on
 # config 2: fp16 bytes are singleton-coded, fewer bytes per lookup; fp32
@@ -74,10 +75,22 @@ class DeviceGroup:
     lanes: tuple            # 4 device addresses (0 where unused)
     out: int
     output: torch.Tensor = field(repr=False, compare=False)
+    tile_words: int = 0     # largest per-tile bitstream copy (tile_copy_words)
 
     @property
     def tiles(self):
         return (self.numel + _native.TILE_ELEMS - 1) // _native.TILE_ELEMS
+
+
+def tile_copy_words(tile_offsets, bit_length):
+    """Largest shared-memory copy of one tile's bitstream, in words: from
+    the 16-byte boundary at or below its first bit through the word four to
+    seven past its last bit (what the kernel copies)."""
+    starts = np.asarray(tile_offsets, dtype=np.int64)
+    if not len(starts):
+        return 0
+    ends = np.append(starts[1:], int(bit_length))
+    return int(((((ends >> 5) + 8) & ~3) - ((starts >> 5) & ~3)).max())
 
 
 @dataclass(frozen=True)
@@ -101,9 +114,10 @@ class TileDecoder:
     def __init__(self):
         self._sm_count = {}
         self._ctas_per_sm = {}
+        self._copy_words = {}
 
     # Reference hook: the staging policy decides the launch geometry.
-    def staging_policy(self, device_index, key_works):
+    def staging_policy(self, device_index, key_works, tile_words=0):
         """Launch geometry for a batch with ``key_works[key] = (tiles,
         layout, raw)`` per (layout, decode table): (warps per CTA,
         {key: works per CTA}).
@@ -118,10 +132,14 @@ class TileDecoder:
         24-warp CTA per SM uses narrower CTAs so that every SM gets work
         (a 24-warp CTA fills an SM's shared memory with the 38 KB table and
         each warp's staging rows and tile-bitstream copy; 8- and 4-warp CTAs
-        run two and three to an SM, 16 and 12 warps)."""
+        run two and three to an SM, 16 and 12 warps). Widths whose
+        per-warp bitstream copy is smaller than the batch's largest tile
+        (``tile_words``) are skipped: such a tile would be read from global
+        memory, several times slower."""
         sms = self._sms(device_index)
         total = sum(n for n, _, _ in key_works.values())
-        nw = next((w for w in CTA_WIDTHS if total >= sms * w), CTA_WIDTHS[-1])
+        fits = [w for w in CTA_WIDTHS if tile_words <= self._tile_words(w)] or list(CTA_WIDTHS)
+        nw = next((w for w in fits if total >= sms * w), fits[-1])
         slots = self._occupancy(device_index, nw) * sms
 
         def per_warp_of(layout, raw):
@@ -140,6 +158,11 @@ class TileDecoder:
         while ctas(plan(units)) > slots:
             units += 1
         return nw, plan(units)
+
+    def _tile_words(self, nw):
+        if nw not in self._copy_words:
+            self._copy_words[nw] = _native.decode_tile_words(nw)
+        return self._copy_words[nw]
 
     def _occupancy(self, device_index, nw):
         """Resident CTAs per SM (CUDA occupancy calculator; shared memory
@@ -205,7 +228,8 @@ class TileDecoder:
         key_works = {key: (sum(groups[i].tiles for i in members[key]), key[0], key[1] == _native.RAW_LUT)
                      for key in keys}
         total_works = sum(n for n, _, _ in key_works.values())
-        nw, per_cta = self.staging_policy(device.index, key_works)
+        tile_words = max((g.tile_words for g in groups if g.lut_index != _native.RAW_LUT), default=0)
+        nw, per_cta = self.staging_policy(device.index, key_works, tile_words)
         works = np.zeros(total_works, dtype=_native.WORK_DTYPE)
         ctas = []
         cursor = 0

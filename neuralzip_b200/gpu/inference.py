@@ -623,6 +623,8 @@ class NeuralZipRuntime:
                 bits=addr("bits"), lens=addr("lens"), tile_off=addr("tile_off"),
                 lanes=tuple(addr(f"lane{lane}") for lane in range(4)),
                 out=output.data_ptr(), output=output,
+                tile_words=gpu_decoder.tile_copy_words(group.encoded.symbols.tile_offsets,
+                                                       group.encoded.symbols.bit_length) if coded else 0,
             )
             uploaded.append(_UploadedGroup(group, device_group))
         by_block = defaultdict(list)

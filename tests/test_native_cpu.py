@@ -221,3 +221,27 @@ def test_config1_storage_round_trip():
 
     export = export_tensors_for_gpu(named, setup)
     assert len(export.groups) == 128 and all(not g.codebook.vocab and g.codebook.max_bits for g in export.groups)
+
+
+def test_decode_geometry_fits_shared_memory():
+    """Each CTA width's shared memory (table + per-warp staging rows and
+    tile-bitstream copy) keeps its resident CTAs within an SM's 228 KB."""
+    resident = {24: 1, 16: 1, 8: 2, 4: 3}
+    copy_words = {24: 956, 16: 1964, 8: 1336, 4: 1296}
+    for nw, ctas in resident.items():
+        smem = _native.decode_smem_bytes(nw)
+        assert smem <= 232448 and ctas * (smem + 1024) <= 233472
+        assert _native.decode_tile_words(nw) == copy_words[nw]
+    with pytest.raises(ValueError):
+        _native.decode_tile_words(12)
+
+
+def test_tile_copy_words_matches_kernel_bounds():
+    from neuralzip_b200.gpu.decoder import tile_copy_words
+
+    # Tiles at bits [0, 100), [100, 5000), [5000, 5001): the copy runs from
+    # the 16-byte boundary at or below the first bit to 4..7 words past the
+    # last one.
+    assert tile_copy_words([0, 100, 5000], 5001) == max(((100 >> 5) + 8) & ~3, (((5000 >> 5) + 8) & ~3) - ((100 >> 5) & ~3),
+                                                         (((5001 >> 5) + 8) & ~3) - ((5000 >> 5) & ~3))
+    assert tile_copy_words([], 0) == 0

@@ -125,10 +125,9 @@ class TileDecoder:
         Every CTA stages one table and runs one layout; its warps take the
         CTA's works in turn, so they get equal counts (+-1). Tiles are
         weighed by their cost relative to a pair-coded bf16 tile
-        (WORK_WEIGHT, RAW_WORK_WEIGHT), and the works per warp are the
-        smallest count whose CTAs fit in one wave of resident CTAs: a launch
-        then ends when its busiest warps do, instead of with a partial last
-        wave that leaves SMs idle. A launch with fewer tiles than one
+        (WORK_WEIGHT, RAW_WORK_WEIGHT), and every resident CTA slot of one
+        wave gets a share of the cost: a launch then ends when its busiest
+        warps do, with no partial last wave and no idle SM. A launch with fewer tiles than one
         24-warp CTA per SM uses narrower CTAs so that every SM gets work
         (a 24-warp CTA fills an SM's shared memory with the 38 KB table and
         each warp's staging rows and tile-bitstream copy; 8- and 4-warp CTAs
@@ -142,22 +141,23 @@ class TileDecoder:
         nw = next((w for w in fits if total >= sms * w), fits[-1])
         slots = self._occupancy(device_index, nw) * sms
 
-        def per_warp_of(layout, raw):
-            """Works per warp-unit of cost, as a divisor of the common count."""
-            return (WORK_WEIGHT[layout] * (1.0 / RAW_WORK_WEIGHT if raw else 1.0))
+        def weight(layout, raw):
+            """Cost of one tile relative to a pair-coded bf16 tile."""
+            return WORK_WEIGHT[layout] * (1.0 / RAW_WORK_WEIGHT if raw else 1.0)
 
-        def plan(units):
-            return {key: max(1, int(round(nw * units / per_warp_of(layout, raw))))
-                    for key, (_, layout, raw) in key_works.items()}
-
-        def ctas(per_cta):
-            return sum(-(-n // per_cta[key]) for key, (n, _, _) in key_works.items())
-
-        cost = sum(n * per_warp_of(layout, raw) for n, layout, raw in key_works.values())
-        units = max(1, -(-int(cost) // (slots * nw)))
-        while ctas(plan(units)) > slots:
-            units += 1
-        return nw, plan(units)
+        # One CTA per key, then each free slot of the wave to the key whose
+        # CTAs carry the most cost each (while it has a tile left for it):
+        # every SM gets a share and the shares are as even as whole tiles
+        # allow; a CTA's warps then take its works in turn (+-1 each).
+        cost = {key: n * weight(layout, raw) for key, (n, layout, raw) in key_works.items()}
+        alloc = {key: 1 for key in key_works}
+        for _ in range(slots - len(alloc)):
+            open_keys = [key for key in alloc if alloc[key] < key_works[key][0]]
+            if not open_keys:
+                break
+            key = max(open_keys, key=lambda k: cost[k] / alloc[k])
+            alloc[key] += 1
+        return nw, {key: -(-key_works[key][0] // alloc[key]) for key in key_works}
 
     def _tile_words(self, nw):
         if nw not in self._copy_words:

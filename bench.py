@@ -464,11 +464,15 @@ def main():
     # them: the bf16 launch alone on `stream` (timed for the roofline), then
     # one launch that mixes the fp16 and fp32 groups.
     others = [b for b in batches if b is not main_batch]
-    sides = [torch.cuda.Stream(device=device) for _ in others]
+    sides = [torch.cuda.Stream(device=device, priority=0) for _ in others]
     fork = torch.cuda.Event()
     joins = [torch.cuda.Event() for _ in others]
 
     def step(times=None):
+        # As nz_decode_launch_many runs them: the bf16 launch first, the
+        # others enqueued at once on low-priority streams (they take SMs as
+        # bf16 CTAs finish).
+        fork.record(stream)
         if times is not None:
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record(stream)
@@ -476,7 +480,6 @@ def main():
         if times is not None:
             b.record(stream)
             times.append((a, b))
-        fork.record(stream)
         for side, join, batch in zip(sides, joins, others):
             side.wait_event(fork)
             decoder.decode_batch(batch, side)
@@ -501,6 +504,18 @@ def main():
     step_ms = max_over_ranks(start.elapsed_time(end) / args.steps, world)
     kernel_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in kernel_events) / len(kernel_events), world)
     clock = clocks.summary()
+    # The bf16 launch alone (no other launch sharing its tail), after the
+    # timed region: the kernel's own rate, for the roofline beside the
+    # in-step one.
+    alone = []
+    for _ in range(max(3, min(args.steps, 50))):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        decoder.decode_batch(main_batch, stream)
+        b.record(stream)
+        alone.append((a, b))
+    torch.cuda.synchronize(device)
+    alone_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in alone) / len(alone), world)
 
     # e2e: pinned host compressed arena -> device -> decode -> pinned host
     # decoded weights, through the public bulk API (pipelined pieces).
@@ -573,7 +588,12 @@ def main():
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind, "traffic": traffic,
                          "kernel": "nz_tile_decode (bf16 launch)",
                          "kernel_ms": round(kernel_ms, 4),
-                         "algorithmic_bytes": int(alg_bytes)},
+                         "algorithmic_bytes": int(alg_bytes),
+                         "alone": {"kernel_ms": round(alone_ms, 4),
+                                   "achieved": round(alg_bytes / (alone_ms * 1e-3) / 1e9, 1),
+                                   "frac": round(alg_bytes / (alone_ms * 1e-3) / 1e9 / peak, 4),
+                                   "note": "the same launch timed by itself after the timed region; in the "
+                                           "step the fp16+fp32 launch shares its tail"}},
             "cpu_baseline": cpu,
             "e2e": e2e,
             "clocks": clock,

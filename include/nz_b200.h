@@ -259,11 +259,11 @@ typedef struct nz_launch {
 int nz_decode_launch(const nz_launch* launch, void* cuda_stream);
 
 /* Several launches (e.g. one per dtype of a block) as one step on
- * `cuda_stream`: the launch with the most warps runs alone on that stream,
- * then the others run side by side on side streams of this library, and
- * the stream waits for all of them. Small launches are latency-bound (one
- * tile per warp), so running them together roughly halves their time. No
- * reference counterpart (the reference launches each layout in turn,
+ * `cuda_stream`: the launch with the most warps goes first on that stream,
+ * the others are enqueued at once on low-priority side streams of this
+ * library (their CTAs take SMs as the first launch's CTAs finish, and run
+ * side by side), and the stream waits for all of them. No reference
+ * counterpart (the reference launches each layout in turn,
  * neuralzip/gpu/inference.py:491-493). */
 int nz_decode_launch_many(const nz_launch* launches, uint32_t count,
                           void* cuda_stream);

@@ -595,7 +595,11 @@ int aux_streams(uint32_t needed, AuxStreams** out) {
     while (aux->streams.size() < needed) {
         cudaStream_t s = nullptr;
         cudaEvent_t e = nullptr;
-        err = cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking);
+        // Lowest priority: when more CTAs wait than SMs are free, the
+        // caller stream's launch is served first.
+        int least = 0, greatest = 0;
+        err = cudaDeviceGetStreamPriorityRange(&least, &greatest);
+        if (err == cudaSuccess) err = cudaStreamCreateWithPriority(&s, cudaStreamNonBlocking, least);
         if (err == cudaSuccess) err = cudaEventCreateWithFlags(&e, cudaEventDisableTiming);
         if (err != cudaSuccess) return nz::fail(NZ_ECUDA, std::string("aux stream: ") + cudaGetErrorString(err));
         aux->streams.push_back(s);
@@ -647,9 +651,11 @@ int nz_decode_launch_many(const nz_launch* launches, uint32_t count, void* cuda_
     if (count == 0) return NZ_OK;
     if (!launches) return nz::fail(NZ_EVALUE, "Null launch descriptors.");
     cudaStream_t stream = reinterpret_cast<cudaStream_t>(cuda_stream);
-    // The launch with the most warps runs alone on the caller's stream (it
-    // fills every SM); the others then run side by side, each on a side
-    // stream, so that small launches, which are latency-bound, share SMs.
+    // The launch with the most warps goes first, on the caller's stream, and
+    // fills every SM; the others are enqueued at once on low-priority side
+    // streams, so their CTAs take SMs as the first launch's CTAs finish (its
+    // tail) and run side by side, small launches being latency-bound. The
+    // caller's stream then waits for all of them.
     uint32_t main = 0;
     for (uint32_t i = 1; i < count; ++i)
         if (launches[i].n_ctas * launches[i].warps_per_cta > launches[main].n_ctas * launches[main].warps_per_cta)
@@ -659,10 +665,10 @@ int nz_decode_launch_many(const nz_launch* launches, uint32_t count, void* cuda_
     int rc = aux_streams(count - 1, &aux);
     if (rc != NZ_OK) return rc;
     std::lock_guard<std::mutex> hold(aux->lock);
-    rc = nz_decode_launch(&launches[main], cuda_stream);
-    if (rc != NZ_OK) return rc;
     cudaError_t err = cudaEventRecord(aux->fork, stream);
     if (err != cudaSuccess) return nz::fail(NZ_ECUDA, std::string("cudaEventRecord: ") + cudaGetErrorString(err));
+    rc = nz_decode_launch(&launches[main], cuda_stream);
+    if (rc != NZ_OK) return rc;
     uint32_t k = 0;
     for (uint32_t i = 0; i < count; ++i) {
         if (i == main) continue;

@@ -91,23 +91,37 @@ __device__ __forceinline__ void stg_u4(void* p, uint32_t a, uint32_t b, uint32_t
 
 // MSB-first window over 32-bit words (bit 31 earliest). The valid bits are
 // the top `avail` bits of hi:lo and everything below them is zero. The next
-// word is requested one refill ahead (pf). The words come from the warp's
-// shared-memory copy of its tile, or from global memory for a tile larger
-// than that copy (a generic pointer serves both): lanes refill at different
-// lookups, and a load's register is tracked for the whole warp, so a refill
-// waits for the loads other lanes issued just before; from shared memory
-// that wait is short. The refill stays a branch: a form without one reads
-// pf on every lookup and so waits for its load there. All shifts are
-// 32-bit funnel shifts.
+// word is requested one refill ahead (pf). kShared: the words come from the
+// warp's shared-memory copy of its tile (32-bit addresses, ld.shared);
+// otherwise from global memory, for a tile larger than that copy. Lanes
+// refill at different lookups, and a load's register is tracked for the
+// whole warp, so a refill waits for the load other lanes issued just
+// before; from shared memory that wait is short. The refill stays a
+// branch: a form without one reads pf on every lookup and so waits for its
+// load there. All shifts are 32-bit funnel shifts.
+template <bool kShared>
 struct Window {
     uint32_t hi, lo, avail, pf;
-    const uint32_t* src;
-    __device__ __forceinline__ void init(const uint32_t* words, uint32_t bitpos) {
-        const uint32_t* p = words + (bitpos >> 5);
+    uint32_t saddr;        // shared: byte address of the next word
+    const uint32_t* gsrc;  // global: the next word
+    __device__ __forceinline__ uint32_t next() {
+        if constexpr (kShared) {
+            uint32_t v;
+            asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(saddr));
+            saddr += 4U;
+            return v;
+        } else {
+            return __ldg(gsrc++);
+        }
+    }
+    // sbase / gbase: shared byte address / global address of the word that
+    // holds bit 0 of `bitpos`'s numbering (the other one is unused).
+    __device__ __forceinline__ void init(uint32_t sbase, const uint32_t* gbase, uint32_t bitpos) {
+        if constexpr (kShared) saddr = sbase + 4U * (bitpos >> 5);
+        else gsrc = gbase + (bitpos >> 5);
         const uint32_t sh = bitpos & 31U;
-        const uint32_t w0 = p[0], w1 = p[1];
-        pf = p[2];
-        src = p + 3;
+        const uint32_t w0 = next(), w1 = next();
+        pf = next();
         hi = __funnelshift_l(w1, w0, sh);
         lo = w1 << sh;
         avail = 64U - sh;
@@ -124,7 +138,7 @@ struct Window {
             hi |= __funnelshift_rc(pf, 0U, avail);
             lo = __funnelshift_rc(0U, pf, avail);
             avail += 32U;
-            pf = *src++;
+            pf = next();
         }
     }
 };
@@ -133,7 +147,8 @@ struct Window {
 // tree one bit at a time (at most 44 steps). Returns a leaf word (byte
 // count in bits 5..7, bytes in 8..23). A table that exceeds the depth sets
 // *status and yields one zero byte, so the lane still finishes.
-__device__ __forceinline__ uint32_t walk_long(const uint32_t* __restrict__ table, uint32_t marker, Window& w,
+template <typename W>
+__device__ __forceinline__ uint32_t walk_long(const uint32_t* __restrict__ table, uint32_t marker, W& w,
                                               int32_t* status) {
     w.consume(NZ_LUT_BITS);
     uint32_t node = (marker >> 16) & kTreeMask;
@@ -164,7 +179,8 @@ __device__ __forceinline__ uint32_t walk_long(const uint32_t* __restrict__ table
 // of one tree step per bit. Otherwise the suffix tree is walked. Returns a
 // leaf word; a table that does not resolve the window sets *status and
 // yields one zero byte.
-__device__ __forceinline__ uint32_t decode_long(const uint32_t* __restrict__ table, uint32_t marker, Window& w,
+template <typename W>
+__device__ __forceinline__ uint32_t decode_long(const uint32_t* __restrict__ table, uint32_t marker, W& w,
                                                 int32_t* status) {
     if (marker & 0x80000000U) return walk_long(table, marker, w, status);
     const uint32_t* canon = table + NZ_LUT_CANON;
@@ -379,7 +395,89 @@ __device__ __forceinline__ void decode_works(const nz_group* __restrict__ groups
         // first bit through four words past its last one (the read-ahead),
         // are copied into the warp's buffer when they fit; inside the stream
         // and its 16-word zero pad.
-        Window win;
+        // Byte queue: `qbits` bits (0, 8, 16 or 24) of decoded bytes wait in
+        // qa between lookups. A lookup's bytes that do not fit in qa are not
+        // kept: when qa fills up it is stored and rebuilt from the entry.
+        uint32_t qa = 0, qbits = 0;
+        uint32_t* row = stage + lane * kStageStride;
+
+        // The tile's rounds, over a window on shared or global memory (two
+        // instantiations, so that each reads its words with its own loads).
+        auto rounds = [&](auto& win) {
+            for (uint32_t r = 0; r < kRounds; ++r) {
+                const uint32_t done = r * kRoundElems;
+                if (__all_sync(0xFFFFFFFFU, n_lane <= done)) break;
+                const uint32_t base = tile_base + done;
+                // bf16/fp16 keep two groups of raw bytes in flight; fp32 (three
+                // raw lanes) loads each group just before it merges, within the
+                // register budget of 64 (8-warp CTAs) to 80 (24-warp CTAs).
+                constexpr bool kAhead = ES == 2;
+                G raw[2];
+                if (kAhead && interior) raw[0].load(lanes, base, 0, lane);
+                const uint32_t want = n_lane > done ? min(kRoundElems, n_lane - done) : 0U;
+                const uint32_t target = (want + 3U) >> 2;
+                for (uint32_t wi = 0; wi < target;) {
+                    const uint2 entry = table2[win.hi >> (32 - NZ_LUT_BITS)];
+                    uint32_t e = entry.x, x = entry.y;
+                    if ((e & 0xFF00U) == 0U) {
+                        const uint32_t leaf = decode_long(table, e, win, status);
+                        e = ((leaf >> 5) & 7U) << 11;
+                        x = leaf >> 8;
+                    }
+                    win.consume(e);
+                    win.top_up();
+                    qa |= x << qbits;
+                    const uint32_t qn = qbits + (e >> 8);  // < 64
+                    if (qn >= 32U) {
+                        row[wi++] = qa;
+                        qa = __funnelshift_l(x, 0U, qbits);
+                    }
+                    qbits = qn & 31U;
+                }
+                __syncwarp();
+                if (interior) {
+                    // Merge the 32 staged rows, kLanesPerRow lanes per row and 8
+                    // elements per lane; each group's raw loads are in flight
+                    // while the previous group merges.
+#pragma unroll
+                    for (uint32_t gi = 0; gi < kGroups; ++gi) {
+                        if (kAhead) {
+                            if (gi + 1 < kGroups) raw[(gi + 1) & 1U].load(lanes, base, gi + 1, lane);
+                        } else {
+                            raw[0].load(lanes, base, gi, lane);
+                        }
+                        raw[kAhead ? (gi & 1U) : 0U].store(out, stage, base, gi, lane);
+                    }
+                } else {
+                    const uint32_t col = (lane % kLanesPerRow) * 8U;
+#pragma unroll
+                    for (uint32_t p0 = 0; p0 < kMergePasses; p0 += G::kGroup) {
+                        uint2 raw[G::kGroup][L::kRawLanes];
+                        uint32_t ex[G::kGroup];
+                        bool full[G::kGroup];
+#pragma unroll
+                        for (uint32_t k = 0; k < G::kGroup; ++k) {
+                            const uint32_t rrow = (p0 + k) * kRowsPerPass + lane / kLanesPerRow;
+                            ex[k] = base + rrow * NZ_LANE_ELEMS + col;
+                            full[k] = vec_ok && ex[k] + 8U <= numel;
+                            if (full[k]) {
+#pragma unroll
+                                for (int l = 0; l < L::kRawLanes; ++l) raw[k][l] = ldg_u2(lanes[l] + ex[k]);
+                            }
+                        }
+#pragma unroll
+                        for (uint32_t k = 0; k < G::kGroup; ++k) {
+                            const uint32_t rrow = (p0 + k) * kRowsPerPass + lane / kLanesPerRow;
+                            const uint32_t* src = stage + rrow * kStageStride + (col >> 2);
+                            const uint32_t x0 = src[0], x1 = src[1];
+                            if (full[k]) L::store8(out, ex[k], raw[k], x0, x1);
+                            else if (ex[k] < numel) merge_tail<ES, REORDER>(out, lanes, ex[k], numel, x0, x1);
+                        }
+                    }
+                }
+                __syncwarp();
+            }
+        };
         {
             const uint32_t* gbits = reinterpret_cast<const uint32_t*>(g.bits);
             const uint32_t wa = (bit0 >> 5) & ~3U;
@@ -397,89 +495,14 @@ __device__ __forceinline__ void decode_works(const nz_group* __restrict__ groups
                 }
                 asm volatile("cp.async.wait_all;" ::: "memory");
                 __syncwarp();
-                win.init(buf - wa, bit0 + incl - len);
+                Window<true> win;
+                win.init(sbuf - 4U * wa, nullptr, bit0 + incl - len);
+                rounds(win);
             } else {
-                win.init(gbits, bit0 + incl - len);
+                Window<false> win;
+                win.init(0U, gbits, bit0 + incl - len);
+                rounds(win);
             }
-        }
-        // Byte queue: `qbits` bits (0, 8, 16 or 24) of decoded bytes wait in
-        // qa between lookups. A lookup's bytes that do not fit in qa are not
-        // kept: when qa fills up it is stored and rebuilt from the entry.
-        uint32_t qa = 0, qbits = 0;
-        uint32_t* row = stage + lane * kStageStride;
-
-        for (uint32_t r = 0; r < kRounds; ++r) {
-            const uint32_t done = r * kRoundElems;
-            if (__all_sync(0xFFFFFFFFU, n_lane <= done)) break;
-            const uint32_t base = tile_base + done;
-            // bf16/fp16 keep two groups of raw bytes in flight; fp32 (three
-            // raw lanes) loads each group just before it merges, within the
-            // 64-register budget.
-            constexpr bool kAhead = ES == 2;
-            G raw[2];
-            if (kAhead && interior) raw[0].load(lanes, base, 0, lane);
-            const uint32_t want = n_lane > done ? min(kRoundElems, n_lane - done) : 0U;
-            const uint32_t target = (want + 3U) >> 2;
-            for (uint32_t wi = 0; wi < target;) {
-                const uint2 entry = table2[win.hi >> (32 - NZ_LUT_BITS)];
-                uint32_t e = entry.x, x = entry.y;
-                if ((e & 0xFF00U) == 0U) {
-                    const uint32_t leaf = decode_long(table, e, win, status);
-                    e = ((leaf >> 5) & 7U) << 11;
-                    x = leaf >> 8;
-                }
-                win.consume(e);
-                win.top_up();
-                qa |= x << qbits;
-                const uint32_t qn = qbits + (e >> 8);  // < 64
-                if (qn >= 32U) {
-                    row[wi++] = qa;
-                    qa = __funnelshift_l(x, 0U, qbits);
-                }
-                qbits = qn & 31U;
-            }
-            __syncwarp();
-            if (interior) {
-                // Merge the 32 staged rows, kLanesPerRow lanes per row and 8
-                // elements per lane; each group's raw loads are in flight
-                // while the previous group merges.
-#pragma unroll
-                for (uint32_t gi = 0; gi < kGroups; ++gi) {
-                    if (kAhead) {
-                        if (gi + 1 < kGroups) raw[(gi + 1) & 1U].load(lanes, base, gi + 1, lane);
-                    } else {
-                        raw[0].load(lanes, base, gi, lane);
-                    }
-                    raw[kAhead ? (gi & 1U) : 0U].store(out, stage, base, gi, lane);
-                }
-            } else {
-                const uint32_t col = (lane % kLanesPerRow) * 8U;
-#pragma unroll
-                for (uint32_t p0 = 0; p0 < kMergePasses; p0 += G::kGroup) {
-                    uint2 raw[G::kGroup][L::kRawLanes];
-                    uint32_t ex[G::kGroup];
-                    bool full[G::kGroup];
-#pragma unroll
-                    for (uint32_t k = 0; k < G::kGroup; ++k) {
-                        const uint32_t rrow = (p0 + k) * kRowsPerPass + lane / kLanesPerRow;
-                        ex[k] = base + rrow * NZ_LANE_ELEMS + col;
-                        full[k] = vec_ok && ex[k] + 8U <= numel;
-                        if (full[k]) {
-#pragma unroll
-                            for (int l = 0; l < L::kRawLanes; ++l) raw[k][l] = ldg_u2(lanes[l] + ex[k]);
-                        }
-                    }
-#pragma unroll
-                    for (uint32_t k = 0; k < G::kGroup; ++k) {
-                        const uint32_t rrow = (p0 + k) * kRowsPerPass + lane / kLanesPerRow;
-                        const uint32_t* src = stage + rrow * kStageStride + (col >> 2);
-                        const uint32_t x0 = src[0], x1 = src[1];
-                        if (full[k]) L::store8(out, ex[k], raw[k], x0, x1);
-                        else if (ex[k] < numel) merge_tail<ES, REORDER>(out, lanes, ex[k], numel, x0, x1);
-                    }
-                }
-            }
-            __syncwarp();
         }
     }
 }

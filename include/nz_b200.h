@@ -228,13 +228,17 @@ typedef struct nz_work {
 #define NZ_LAYOUT_FP32 2u
 
 /* One CTA: a contiguous range of works sharing one decode table and one
- * element layout. */
+ * element layout. With launch scratch (nz_launch.scratch), the CTAs that
+ * name the same queue share their range: each warp claims the range's
+ * next work from the queue's counter, so those CTAs finish together. */
 typedef struct nz_cta {
     uint32_t lut;        /* index into luts, or NZ_RAW_LUT */
     uint32_t begin;
     uint32_t end;
     uint16_t lut_words;  /* words of the table to stage (<= NZ_LUT_WORDS) */
     uint16_t layout;     /* NZ_LAYOUT_* of every group of the range */
+    uint32_t queue;      /* counter index in the launch scratch (< queues) */
+    uint32_t reserved;   /* zero */
 } nz_cta;
 
 /* Replaces CuPyDecoder.decode_batch (neuralzip/gpu/decoder.py:193-208) and
@@ -250,11 +254,18 @@ typedef struct nz_cta {
 typedef struct nz_launch {
     uint32_t warps_per_cta;
     uint32_t n_ctas;
-    uint64_t groups;  /* const nz_group* */
-    uint64_t works;   /* const nz_work* */
-    uint64_t ctas;    /* const nz_cta* */
-    uint64_t luts;    /* const uint64_t* */
-    uint64_t status;  /* int32_t* */
+    uint64_t groups;   /* const nz_group* */
+    uint64_t works;    /* const nz_work* */
+    uint64_t ctas;     /* const nz_cta* */
+    uint64_t luts;     /* const uint64_t* */
+    uint64_t status;   /* int32_t* */
+    /* uint32_t[queues + 1], zero before the first launch that uses it; the
+     * launch's last CTA sets it back to zero. 0: no queues, each CTA
+     * decodes its own range. Launches that share scratch must not overlap
+     * on the GPU. */
+    uint64_t scratch;
+    uint32_t queues;
+    uint32_t reserved; /* zero */
 } nz_launch;
 int nz_decode_launch(const nz_launch* launch, void* cuda_stream);
 

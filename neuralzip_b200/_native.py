@@ -32,7 +32,7 @@ LUT_WORDS = LUT_TREE + 2 * TREE_MAX_NODES
 MAX_CODE_BITS = 56
 BITS_PAD_WORDS = 16
 RAW_LUT = 0xFFFFFFFF
-ABI_VERSION = 3
+ABI_VERSION = 4
 LAYOUT_BF16, LAYOUT_FP16, LAYOUT_FP32 = 0, 1, 2
 
 OK, EVALUE, ETYPE, EOVERFLOW, ERUNTIME, ECUDA = range(6)
@@ -64,15 +64,17 @@ class PackJob(ctypes.Structure):
 class Launch(ctypes.Structure):
     _fields_ = [("warps_per_cta", ctypes.c_uint32), ("n_ctas", ctypes.c_uint32), ("groups", ctypes.c_uint64),
                 ("works", ctypes.c_uint64), ("ctas", ctypes.c_uint64), ("luts", ctypes.c_uint64),
-                ("status", ctypes.c_uint64)]
+                ("status", ctypes.c_uint64), ("scratch", ctypes.c_uint64), ("queues", ctypes.c_uint32),
+                ("reserved", ctypes.c_uint32)]
 
 
 # Device descriptor records (numpy views of the C structs).
 GROUP_DTYPE = np.dtype([("bits", "<u8"), ("lens", "<u8"), ("tile_off", "<u8"), ("lanes", "<u8", (4,)),
                         ("out", "<u8"), ("numel", "<u4"), ("lut", "<u4")])
 WORK_DTYPE = np.dtype([("group", "<u4"), ("tile", "<u4")])
-CTA_DTYPE = np.dtype([("lut", "<u4"), ("begin", "<u4"), ("end", "<u4"), ("lut_words", "<u2"), ("layout", "<u2")])
-assert GROUP_DTYPE.itemsize == 72 and WORK_DTYPE.itemsize == 8 and CTA_DTYPE.itemsize == 16
+CTA_DTYPE = np.dtype([("lut", "<u4"), ("begin", "<u4"), ("end", "<u4"), ("lut_words", "<u2"), ("layout", "<u2"),
+                      ("queue", "<u4"), ("reserved", "<u4")])
+assert GROUP_DTYPE.itemsize == 72 and WORK_DTYPE.itemsize == 8 and CTA_DTYPE.itemsize == 24
 
 EXPORTS = (
     "nz_export_code_table", "nz_codebook_create", "nz_codebook_destroy", "nz_codebook_info",

@@ -311,7 +311,8 @@ template <int ES, bool REORDER, int NW>
 __device__ __forceinline__ void decode_works(const nz_group* __restrict__ groups,
                                              const nz_work* __restrict__ works, uint32_t begin,
                                              uint32_t end, const uint32_t* __restrict__ table,
-                                             uint32_t* stage, int32_t* __restrict__ status) {
+                                             uint32_t* stage, int32_t* __restrict__ status,
+                                             uint32_t* __restrict__ queue) {
     constexpr uint32_t kBitBufWords = bit_buf_words(NW);
     using L = Layout<ES, REORDER>;
     using G = MergeGroup<ES, REORDER>;
@@ -319,7 +320,25 @@ __device__ __forceinline__ void decode_works(const nz_group* __restrict__ groups
     const uint32_t warp = threadIdx.x >> 5;
     const uint32_t lane = threadIdx.x & 31U;
     const uint2* table2 = reinterpret_cast<const uint2*>(table);
-    for (uint32_t w = begin + warp; w < end; w += NW) {
+    // Without a queue the warps take the CTA's works in turn. With one, each
+    // warp claims the next work of the range shared by the queue's CTAs
+    // (lane 0, one atomic per work), the next claim issued halfway through
+    // the current work so that the atomic's round trip is hidden.
+    uint32_t w = begin + warp;
+    if (queue) {
+        uint32_t first = 0;
+        if (lane == 0) first = atomicAdd(queue, 1U);
+        w = begin + __shfl_sync(0xFFFFFFFFU, first, 0);
+    }
+    while (w < end) {
+        uint32_t claim = 0;    // lane 0: the next claimed index
+        bool claimed = false;  // warp-uniform
+        auto claim_next = [&]() {
+            if (queue && !claimed) {
+                if (lane == 0) claim = atomicAdd(queue, 1U);
+                claimed = true;
+            }
+        };
         const nz_work item = works[w];
         const nz_group& g = groups[item.group];
         const uint32_t numel = g.numel;
@@ -334,6 +353,7 @@ __device__ __forceinline__ void decode_works(const nz_group* __restrict__ groups
         const uint32_t tile_base = item.tile * NZ_TILE_ELEMS;
 
         if (g.lut == NZ_RAW_LUT) {
+            claim_next();
             // Raw fragment: the selected lane is stored as bytes.
             const uint8_t* sel = lanes[L::kSel];
             const bool sel_ok = vec_ok && (reinterpret_cast<uint64_t>(sel) & 15U) == 0;
@@ -357,6 +377,7 @@ __device__ __forceinline__ void decode_works(const nz_group* __restrict__ groups
                     merge_tail<ES, REORDER>(out, lanes, e, numel, x0, x1);
                 }
             }
+            w = queue ? begin + __shfl_sync(0xFFFFFFFFU, claim, 0) : w + NW;
             continue;
         }
 
@@ -414,6 +435,7 @@ __device__ __forceinline__ void decode_works(const nz_group* __restrict__ groups
                 constexpr bool kAhead = ES == 2;
                 G raw[2];
                 if (kAhead && interior) raw[0].load(lanes, base, 0, lane);
+                if (r + 1 == kRounds) claim_next();
                 const uint32_t want = n_lane > done ? min(kRoundElems, n_lane - done) : 0U;
                 const uint32_t target = (want + 3U) >> 2;
                 for (uint32_t wi = 0; wi < target;) {
@@ -504,6 +526,8 @@ __device__ __forceinline__ void decode_works(const nz_group* __restrict__ groups
                 rounds(win);
             }
         }
+        claim_next();  // a tile that ended before its last round
+        w = queue ? begin + __shfl_sync(0xFFFFFFFFU, claim, 0) : w + NW;
     }
 }
 
@@ -516,12 +540,13 @@ template <int NW>
 __global__ void __launch_bounds__(NW * 32, ctas_per_sm(NW))
     nz_tile_decode(const nz_group* __restrict__ groups, const nz_work* __restrict__ works,
                    const nz_cta* __restrict__ ctas, const uint64_t* __restrict__ luts,
-                   int32_t* __restrict__ status) {
+                   int32_t* __restrict__ status, uint32_t* __restrict__ scratch, uint32_t queues) {
     extern __shared__ __align__(16) uint32_t smem[];
     uint32_t* table = smem;
     uint32_t* stage = smem + NZ_LUT_WORDS + (threadIdx.x >> 5) * warp_words(NW);
 
     const nz_cta cta = ctas[blockIdx.x];
+    uint32_t* queue = scratch && cta.queue < queues ? scratch + cta.queue : nullptr;
     if (cta.lut != NZ_RAW_LUT) {
         const uint4* src = reinterpret_cast<const uint4*>(luts[cta.lut]);
         uint4* dst = reinterpret_cast<uint4*>(table);
@@ -531,16 +556,29 @@ __global__ void __launch_bounds__(NW * 32, ctas_per_sm(NW))
     __syncthreads();
     switch (cta.layout) {
         case NZ_LAYOUT_BF16:
-            decode_works<2, true, NW>(groups, works, cta.begin, cta.end, table, stage, status);
+            decode_works<2, true, NW>(groups, works, cta.begin, cta.end, table, stage, status, queue);
             break;
         case NZ_LAYOUT_FP16:
-            decode_works<2, false, NW>(groups, works, cta.begin, cta.end, table, stage, status);
+            decode_works<2, false, NW>(groups, works, cta.begin, cta.end, table, stage, status, queue);
             break;
         case NZ_LAYOUT_FP32:
-            decode_works<4, true, NW>(groups, works, cta.begin, cta.end, table, stage, status);
+            decode_works<4, true, NW>(groups, works, cta.begin, cta.end, table, stage, status, queue);
             break;
         default:
             if (threadIdx.x == 0 && status) *status = kStatusBadLayout;
+    }
+    if (scratch) {
+        // The launch's last CTA to finish sets the queue counters back to
+        // zero for the next launch that uses this scratch.
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            __threadfence();
+            if (atomicAdd(scratch + queues, 1U) == gridDim.x - 1U) {
+                for (uint32_t q = 0; q < queues; ++q) scratch[q] = 0U;
+                scratch[queues] = 0U;
+                __threadfence();
+            }
+        }
     }
 }
 
@@ -568,7 +606,7 @@ cudaError_t launch_one(const nz_launch& l, cudaStream_t stream) {
     nz_tile_decode<NW><<<l.n_ctas, NW * 32, smem_bytes<NW>(), stream>>>(
         reinterpret_cast<const nz_group*>(l.groups), reinterpret_cast<const nz_work*>(l.works),
         reinterpret_cast<const nz_cta*>(l.ctas), reinterpret_cast<const uint64_t*>(l.luts),
-        reinterpret_cast<int32_t*>(l.status));
+        reinterpret_cast<int32_t*>(l.status), reinterpret_cast<uint32_t*>(l.scratch), l.queues);
     return cudaGetLastError();
 }
 

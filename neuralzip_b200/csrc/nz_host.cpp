@@ -507,7 +507,7 @@ int nz_last_error(char* buf, size_t cap) {
     return NZ_OK;
 }
 
-int nz_abi_version(void) { return 3; }
+int nz_abi_version(void) { return 4; }
 
 int nz_codebook_create(const uint8_t* lengths, const uint64_t* values, uint32_t nsym,
                        const uint8_t* vocab, uint32_t vocab_size, nz_codebook** out) {

@@ -111,6 +111,14 @@ class PreparedBatch:
 class TileDecoder:
     """Host side of the sm_100a tile decode kernel."""
 
+    # Whether the CTAs of one (layout, table) key share its works through a
+    # queue counter in launch scratch (they then finish together), or each
+    # takes a fixed range. Fixed ranges are the default: on config 2 the
+    # queues made the bf16 launch 3% slower (0.760 against 0.738 ms), the
+    # one-wave plan being balanced already; queues suit launches whose tiles
+    # differ in cost.
+    work_queues = False
+
     def __init__(self):
         self._sm_count = {}
         self._ctas_per_sm = {}
@@ -120,7 +128,7 @@ class TileDecoder:
     def staging_policy(self, device_index, key_works, tile_words=0):
         """Launch geometry for a batch with ``key_works[key] = (tiles,
         layout, raw)`` per (layout, decode table): (warps per CTA,
-        {key: works per CTA}).
+        {key: CTAs}).
 
         Every CTA stages one table and runs one layout; its warps take the
         CTA's works in turn, so they get equal counts (+-1). Tiles are
@@ -157,7 +165,7 @@ class TileDecoder:
                 break
             key = max(open_keys, key=lambda k: cost[k] / alloc[k])
             alloc[key] += 1
-        return nw, {key: -(-key_works[key][0] // alloc[key]) for key in key_works}
+        return nw, alloc
 
     def _tile_words(self, nw):
         if nw not in self._copy_words:
@@ -229,11 +237,11 @@ class TileDecoder:
                      for key in keys}
         total_works = sum(n for n, _, _ in key_works.values())
         tile_words = max((g.tile_words for g in groups if g.lut_index != _native.RAW_LUT), default=0)
-        nw, per_cta = self.staging_policy(device.index, key_works, tile_words)
+        nw, key_ctas = self.staging_policy(device.index, key_works, tile_words)
         works = np.zeros(total_works, dtype=_native.WORK_DTYPE)
         ctas = []
         cursor = 0
-        for key in keys:
+        for queue, key in enumerate(keys):
             layout, lut = key
             begin = cursor
             for i in members[key]:
@@ -243,9 +251,14 @@ class TileDecoder:
                 cursor += n
             slot = _native.RAW_LUT if lut == _native.RAW_LUT else lut_slot[lut]
             words = 0 if lut == _native.RAW_LUT else lut_words[lut]
-            step = max(1, int(per_cta[key]))
-            for start in range(begin, cursor, step):
-                ctas.append((slot, start, min(cursor, start + step), words, layout))
+            n_ctas = max(1, int(key_ctas[key]))
+            if self.work_queues:
+                # The key's CTAs share its range through one queue counter.
+                ctas.extend((slot, begin, cursor, words, layout, queue, 0) for _ in range(n_ctas))
+            else:
+                step = -(-(cursor - begin) // n_ctas)
+                for start in range(begin, cursor, step):
+                    ctas.append((slot, start, min(cursor, start + step), words, layout, 0, 0))
         cta_array = np.array(ctas, dtype=_native.CTA_DTYPE)
         if not len(lut_ptrs):
             lut_ptrs = np.zeros(1, dtype=np.uint64)
@@ -259,6 +272,12 @@ class TileDecoder:
         launch.groups, launch.works, launch.ctas, launch.luts = (t.data_ptr() for t in tensors)
         launch.status = status.data_ptr()
         launch.n_ctas = len(cta_array)
+        if self.work_queues:
+            # One counter per key plus the launch's finished-CTA count; the
+            # kernel sets them back to zero at the end of each launch.
+            scratch = torch.zeros(len(keys) + 1, dtype=torch.int32, device=device)
+            tensors = tensors + (scratch,)
+            launch.scratch, launch.queues = scratch.data_ptr(), len(keys)
         return PreparedBatch(
             descriptor_tensors=tensors, device=device, layout=tuple(sorted(set(layouts))), warps_per_cta=nw,
             shared_memory=shared_memory_bytes(nw), kernel_grid=(len(cta_array),), launch=launch,

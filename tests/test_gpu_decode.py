@@ -205,7 +205,7 @@ def test_c_abi_launch_by_hand():
     groups = np.zeros(1, dtype=_native.GROUP_DTYPE)
     groups[0] = (dg.bits, dg.lens, dg.tile_off, dg.lanes, dg.out, numel, 0)
     works = np.array([(0, t) for t in range(dg.tiles)], dtype=_native.WORK_DTYPE)
-    ctas = np.array([(0, 0, dg.tiles, dg.lut_words, _native.LAYOUT_FP32)], dtype=_native.CTA_DTYPE)
+    ctas = np.array([(0, 0, dg.tiles, dg.lut_words, _native.LAYOUT_FP32, 0, 0)], dtype=_native.CTA_DTYPE)
     luts = np.array([dg.lut_ptr], dtype=np.uint64)
     dev = [torch.from_numpy(a.view(np.uint8).copy()).cuda() for a in (groups, works, ctas, luts)]
     status = torch.zeros(1, dtype=torch.int32, device="cuda")
@@ -226,6 +226,71 @@ def test_c_abi_launch_by_hand():
     torch.cuda.synchronize()
     assert int(status.item()) == 3
     assert bool((out.view(torch.int32) == -1).all())
+
+
+def test_c_abi_work_queues_by_hand():
+    """CTAs that name one queue share their range through the launch
+    scratch: every tile is decoded once, and the last CTA sets the counters
+    back to zero, so the next launch on the same scratch works too."""
+    spec = DTYPES[torch.bfloat16]
+    numel = 9 * 8192 + 77
+    raw = H.gaussian_raw(numel, 0.02, torch.bfloat16, 5)
+    sel = H.selected_lane(raw, spec)
+    lengths, vocab = H.mixed_book_for(sel)
+    book = GPUCodebook(tuple(lengths), tuple(int(v) for v in O.mixed_codes(lengths)), vocab)
+    out = torch.empty(numel, dtype=torch.bfloat16, device="cuda")
+    arena = []
+    dg = _device_group(raw, spec, book, out, arena)
+    groups = np.zeros(1, dtype=_native.GROUP_DTYPE)
+    groups[0] = (dg.bits, dg.lens, dg.tile_off, dg.lanes, dg.out, numel, 0)
+    works = np.array([(0, t) for t in range(dg.tiles)], dtype=_native.WORK_DTYPE)
+    ctas = np.array([(0, 0, dg.tiles, dg.lut_words, _native.LAYOUT_BF16, 0, 0)] * 3, dtype=_native.CTA_DTYPE)
+    luts = np.array([dg.lut_ptr], dtype=np.uint64)
+    dev = [torch.from_numpy(a.view(np.uint8).copy()).cuda() for a in (groups, works, ctas, luts)]
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    scratch = torch.zeros(2, dtype=torch.int32, device="cuda")
+    launch = _native.Launch()
+    launch.warps_per_cta = 4
+    launch.groups, launch.works, launch.ctas, launch.luts = (t.data_ptr() for t in dev)
+    launch.status = status.data_ptr()
+    launch.n_ctas = 3
+    launch.scratch, launch.queues = scratch.data_ptr(), 1
+    for _ in range(3):
+        out.view(torch.int16).fill_(-1)
+        _native.decode_launch(launch, torch.cuda.current_stream().cuda_stream)
+        torch.cuda.synchronize()
+        assert bytes(out.cpu().view(torch.uint8).numpy()) == raw
+        assert int(status.item()) == 0
+        assert scratch.tolist() == [0, 0]
+
+
+@pytest.mark.parametrize("work_queues", [False, True])
+def test_fixed_ranges_and_work_queues_decode_alike(work_queues):
+    """The launch plan with per-CTA ranges and with shared queues gives the
+    same bits over a batch of several codebooks, twice in a row."""
+    spec = DTYPES[torch.bfloat16]
+    decoder = gpu_decoder.TileDecoder()
+    decoder.work_queues = work_queues
+    outs, devs, raws, arena = [], [], [], []
+    for seed, sigma in enumerate((0.02, 0.5, 0.002)):
+        numel = (5 + seed) * 8192 + 31 * seed
+        raw = H.gaussian_raw(numel, sigma, torch.bfloat16, 10 + seed)
+        sel = H.selected_lane(raw, spec)
+        lengths, vocab = H.mixed_book_for(sel)
+        book = GPUCodebook(tuple(lengths), tuple(int(v) for v in O.mixed_codes(lengths)), vocab)
+        out = torch.empty(numel, dtype=torch.bfloat16, device="cuda")
+        devs.append(_device_group(raw, spec, book, out, arena, lut_index=seed))
+        outs.append(out)
+        raws.append(raw)
+    batch = decoder.prepare_batch(devs)
+    for _ in range(2):
+        for out in outs:
+            out.view(torch.int16).fill_(-1)
+        decoder.decode_batch(batch)
+        torch.cuda.synchronize()
+        decoder.check_status(batch)
+        for out, raw in zip(outs, raws):
+            assert bytes(out.cpu().view(torch.uint8).numpy()) == raw
 
 
 def test_launch_rejects_bad_geometry():

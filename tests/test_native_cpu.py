@@ -27,7 +27,7 @@ def test_library_exports_every_declared_symbol():
     lib = ctypes.CDLL(str(_native.library_path()))
     for name in declared:
         assert hasattr(lib, name), name
-    assert _native.load().nz_abi_version() == _native.ABI_VERSION == 3
+    assert _native.load().nz_abi_version() == _native.ABI_VERSION == 4
 
 
 def test_struct_layouts_match_header(tmp_path):

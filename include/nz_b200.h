@@ -269,6 +269,7 @@ typedef struct nz_launch {
 } nz_launch;
 int nz_decode_launch(const nz_launch* launch, void* cuda_stream);
 
+
 /* Several launches (e.g. one per dtype of a block) as one step on
  * `cuda_stream`: the launch with the most warps goes first on that stream,
  * the others are enqueued at once on low-priority side streams of this

@@ -307,7 +307,7 @@ struct MergeGroup {
 
 // The works [begin, end) of one CTA, taken in turn by its NW warps, for
 // one element layout. `table` is the CTA's staged decode table.
-template <int ES, bool REORDER, int NW>
+template <int ES, bool REORDER, int NW, bool kQueue>
 __device__ __forceinline__ void decode_works(const nz_group* __restrict__ groups,
                                              const nz_work* __restrict__ works, uint32_t begin,
                                              uint32_t end, const uint32_t* __restrict__ table,
@@ -325,7 +325,8 @@ __device__ __forceinline__ void decode_works(const nz_group* __restrict__ groups
     // (lane 0, one atomic per work), the next claim issued halfway through
     // the current work so that the atomic's round trip is hidden.
     uint32_t w = begin + warp;
-    if (queue) {
+    if (kQueue && !queue) return;  // see nz_tile_decode
+    if constexpr (kQueue) {
         uint32_t first = 0;
         if (lane == 0) first = atomicAdd(queue, 1U);
         w = begin + __shfl_sync(0xFFFFFFFFU, first, 0);
@@ -334,9 +335,11 @@ __device__ __forceinline__ void decode_works(const nz_group* __restrict__ groups
         uint32_t claim = 0;    // lane 0: the next claimed index
         bool claimed = false;  // warp-uniform
         auto claim_next = [&]() {
-            if (queue && !claimed) {
-                if (lane == 0) claim = atomicAdd(queue, 1U);
-                claimed = true;
+            if constexpr (kQueue) {
+                if (!claimed) {
+                    if (lane == 0) claim = atomicAdd(queue, 1U);
+                    claimed = true;
+                }
             }
         };
         const nz_work item = works[w];
@@ -377,7 +380,7 @@ __device__ __forceinline__ void decode_works(const nz_group* __restrict__ groups
                     merge_tail<ES, REORDER>(out, lanes, e, numel, x0, x1);
                 }
             }
-            w = queue ? begin + __shfl_sync(0xFFFFFFFFU, claim, 0) : w + NW;
+            w = kQueue ? begin + __shfl_sync(0xFFFFFFFFU, claim, 0) : w + NW;
             continue;
         }
 
@@ -527,7 +530,7 @@ __device__ __forceinline__ void decode_works(const nz_group* __restrict__ groups
             }
         }
         claim_next();  // a tile that ended before its last round
-        w = queue ? begin + __shfl_sync(0xFFFFFFFFU, claim, 0) : w + NW;
+        w = kQueue ? begin + __shfl_sync(0xFFFFFFFFU, claim, 0) : w + NW;
     }
 }
 
@@ -536,7 +539,10 @@ constexpr int32_t kStatusBadLayout = 3;
 // One launch covers CTAs of every element layout: each CTA stages its
 // decode table and runs the body of its layout (uniform per CTA, so the
 // switch does not diverge).
-template <int NW>
+// kQueue: the launch has work-queue scratch (its CTAs share ranges);
+// fixed ranges and queues are separate kernels, so that neither path
+// carries the other's registers.
+template <int NW, bool kQueue>
 __global__ void __launch_bounds__(NW * 32, ctas_per_sm(NW))
     nz_tile_decode(const nz_group* __restrict__ groups, const nz_work* __restrict__ works,
                    const nz_cta* __restrict__ ctas, const uint64_t* __restrict__ luts,
@@ -546,7 +552,8 @@ __global__ void __launch_bounds__(NW * 32, ctas_per_sm(NW))
     uint32_t* stage = smem + NZ_LUT_WORDS + (threadIdx.x >> 5) * warp_words(NW);
 
     const nz_cta cta = ctas[blockIdx.x];
-    uint32_t* queue = scratch && cta.queue < queues ? scratch + cta.queue : nullptr;
+    // A CTA whose queue index is out of range takes its own range.
+    uint32_t* queue = kQueue && cta.queue < queues ? scratch + cta.queue : nullptr;
     if (cta.lut != NZ_RAW_LUT) {
         const uint4* src = reinterpret_cast<const uint4*>(luts[cta.lut]);
         uint4* dst = reinterpret_cast<uint4*>(table);
@@ -556,18 +563,18 @@ __global__ void __launch_bounds__(NW * 32, ctas_per_sm(NW))
     __syncthreads();
     switch (cta.layout) {
         case NZ_LAYOUT_BF16:
-            decode_works<2, true, NW>(groups, works, cta.begin, cta.end, table, stage, status, queue);
+            decode_works<2, true, NW, kQueue>(groups, works, cta.begin, cta.end, table, stage, status, queue);
             break;
         case NZ_LAYOUT_FP16:
-            decode_works<2, false, NW>(groups, works, cta.begin, cta.end, table, stage, status, queue);
+            decode_works<2, false, NW, kQueue>(groups, works, cta.begin, cta.end, table, stage, status, queue);
             break;
         case NZ_LAYOUT_FP32:
-            decode_works<4, true, NW>(groups, works, cta.begin, cta.end, table, stage, status, queue);
+            decode_works<4, true, NW, kQueue>(groups, works, cta.begin, cta.end, table, stage, status, queue);
             break;
         default:
             if (threadIdx.x == 0 && status) *status = kStatusBadLayout;
     }
-    if (scratch) {
+    if constexpr (kQueue) {
         // The launch's last CTA to finish sets the queue counters back to
         // zero for the next launch that uses this scratch.
         __syncthreads();
@@ -588,26 +595,31 @@ constexpr size_t smem_bytes() {
 }
 
 // Opts the instantiation into its dynamic shared memory (once per process).
-template <int NW>
+template <int NW, bool kQueue>
 cudaError_t ensure_smem_attribute() {
     static std::once_flag once;
     static cudaError_t err = cudaSuccess;
     std::call_once(once, [&]() {
-        err = cudaFuncSetAttribute(nz_tile_decode<NW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        err = cudaFuncSetAttribute(nz_tile_decode<NW, kQueue>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    static_cast<int>(smem_bytes<NW>()));
     });
     return err;
 }
 
-template <int NW>
-cudaError_t launch_one(const nz_launch& l, cudaStream_t stream) {
-    const cudaError_t attr_err = ensure_smem_attribute<NW>();
+template <int NW, bool kQueue>
+cudaError_t launch_kernel(const nz_launch& l, cudaStream_t stream) {
+    const cudaError_t attr_err = ensure_smem_attribute<NW, kQueue>();
     if (attr_err != cudaSuccess) return attr_err;
-    nz_tile_decode<NW><<<l.n_ctas, NW * 32, smem_bytes<NW>(), stream>>>(
+    nz_tile_decode<NW, kQueue><<<l.n_ctas, NW * 32, smem_bytes<NW>(), stream>>>(
         reinterpret_cast<const nz_group*>(l.groups), reinterpret_cast<const nz_work*>(l.works),
         reinterpret_cast<const nz_cta*>(l.ctas), reinterpret_cast<const uint64_t*>(l.luts),
         reinterpret_cast<int32_t*>(l.status), reinterpret_cast<uint32_t*>(l.scratch), l.queues);
     return cudaGetLastError();
+}
+
+template <int NW>
+cudaError_t launch_one(const nz_launch& l, cudaStream_t stream) {
+    return l.scratch ? launch_kernel<NW, true>(l, stream) : launch_kernel<NW, false>(l, stream);
 }
 
 cudaError_t launch_nw(const nz_launch& l, cudaStream_t stream) {
@@ -621,9 +633,10 @@ cudaError_t launch_nw(const nz_launch& l, cudaStream_t stream) {
 
 template <int NW>
 cudaError_t occupancy_one(int* ctas) {
-    const cudaError_t err = ensure_smem_attribute<NW>();
+    const cudaError_t err = ensure_smem_attribute<NW, false>();
     if (err != cudaSuccess) return err;
-    return cudaOccupancyMaxActiveBlocksPerMultiprocessor(ctas, nz_tile_decode<NW>, NW * 32, smem_bytes<NW>());
+    return cudaOccupancyMaxActiveBlocksPerMultiprocessor(ctas, nz_tile_decode<NW, false>, NW * 32,
+                                                         smem_bytes<NW>());
 }
 
 // Side streams of nz_decode_launch_many, per device, created on first use

@@ -112,12 +112,10 @@ class TileDecoder:
     """Host side of the sm_100a tile decode kernel."""
 
     # Whether the CTAs of one (layout, table) key share its works through a
-    # queue counter in launch scratch (they then finish together), or each
-    # takes a fixed range. Fixed ranges are the default: on config 2 the
-    # queues made the bf16 launch 3% slower (0.760 against 0.738 ms), the
-    # one-wave plan being balanced already; queues suit launches whose tiles
-    # differ in cost.
-    work_queues = False
+    # queue counter in launch scratch (they then finish together: on config
+    # 2 the bf16 launch takes 0.698 ms against 0.727 ms with a fixed range
+    # per CTA), or each CTA takes a fixed range (no scratch).
+    work_queues = True
 
     def __init__(self):
         self._sm_count = {}

@@ -269,6 +269,22 @@ typedef struct nz_launch {
 } nz_launch;
 int nz_decode_launch(const nz_launch* launch, void* cuda_stream);
 
+/* nz_decode_launch with work queues whose counters live in this library's
+ * own device memory, for callers that cannot allocate device memory: a
+ * plugin inside a serving process whose memory pool has reserved all of
+ * HBM, or a host path that must not call cudaMalloc because it may
+ * synchronize the device. It allocates nothing; the caller still passes
+ * every input and output. launch->scratch is ignored and launch->queues
+ * must be at most 1024 (NZ_EVALUE otherwise); the CTAs name their queues
+ * as for nz_decode_launch. The counters (4 KB per GPU that loads the
+ * library, held until the process exits) are looked up and cleared by the
+ * first call on each device, which should therefore come before any stream
+ * capture; each launch's last CTA sets them back to zero. All calls on
+ * one GPU share them, so calls that overlap on that GPU (streams with no
+ * order between them) race and must not be issued. No counterpart in the
+ * reference, whose decoder allocates its own buffers
+ * (neuralzip/gpu/decoder.py). */
+int nz_decode_launch_noalloc(const nz_launch* launch, void* cuda_stream);
 
 /* Several launches (e.g. one per dtype of a block) as one step on
  * `cuda_stream`: the launch with the most warps goes first on that stream,

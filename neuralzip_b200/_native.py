@@ -80,7 +80,7 @@ EXPORTS = (
     "nz_export_code_table", "nz_codebook_create", "nz_codebook_destroy", "nz_codebook_info",
     "nz_codebook_lut", "nz_codebook_table_words", "nz_huff0_build", "nz_huff0_read", "nz_pack_bound", "nz_pack_chunk",
     "nz_pack_many", "nz_split_lanes", "nz_exponent_histograms", "nz_count_tokens", "nz_mixed_encode", "nz_mixed_decode",
-    "nz_huff0_encode", "nz_huff0_decode", "nz_decode_launch", "nz_decode_launch_many", "nz_decode_occupancy", "nz_decode_smem_bytes",
+    "nz_huff0_encode", "nz_huff0_decode", "nz_decode_launch", "nz_decode_launch_noalloc", "nz_decode_launch_many", "nz_decode_occupancy", "nz_decode_smem_bytes",
     "nz_decode_tile_words",
     "nz_schedule_create", "nz_schedule_destroy", "nz_schedule_enter", "nz_schedule_decode_unit",
     "nz_schedule_drain", "nz_schedule_mark", "nz_last_error",
@@ -138,6 +138,7 @@ def _declare(lib):
         "nz_huff0_encode": [c.c_void_p, c.c_void_p, c.c_uint64, c.c_void_p, c.c_uint64, u64p],
         "nz_huff0_decode": [c.c_void_p, c.c_void_p, c.c_uint64, c.c_void_p, c.c_uint64],
         "nz_decode_launch": [c.POINTER(Launch), c.c_void_p],
+        "nz_decode_launch_noalloc": [c.POINTER(Launch), c.c_void_p],
         "nz_decode_occupancy": [c.c_uint32, u32p],
         "nz_decode_launch_many": [c.POINTER(Launch), c.c_uint32, c.c_void_p],
         "nz_schedule_create": [c.POINTER(Launch), u32p, c.c_uint32, c.c_uint32, c.c_void_p, c.POINTER(c.c_void_p)],
@@ -457,3 +458,11 @@ def decode_launch(launch, stream_handle):
     """Enqueues the tile decode on a CUDA stream handle (an int)."""
     lib = load()
     check(lib.nz_decode_launch(ctypes.byref(launch), ctypes.c_void_p(int(stream_handle) or None)))
+
+
+def decode_launch_noalloc(launch, stream_handle):
+    """nz_decode_launch_noalloc: the same decode, its work-queue counters in
+    the library's own device memory (for callers that cannot allocate);
+    launch.scratch is ignored."""
+    lib = load()
+    check(lib.nz_decode_launch_noalloc(ctypes.byref(launch), ctypes.c_void_p(int(stream_handle) or None)))

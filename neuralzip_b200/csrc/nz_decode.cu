@@ -683,6 +683,37 @@ int aux_streams(uint32_t needed, AuxStreams** out) {
     return NZ_OK;
 }
 
+// Work-queue counters of nz_decode_launch_noalloc, in the library's own
+// device memory: every GPU that loads this library holds this array until
+// the process exits. kNoAllocQueues counters plus the finished-CTA count.
+constexpr uint32_t kNoAllocQueues = 1024;
+static __device__ __align__(256) uint32_t g_noalloc_scratch[kNoAllocQueues + 1];
+
+// Device address of g_noalloc_scratch on the current device, looked up (and
+// the counters cleared) on the first call per device. In host code the
+// array's name is only a host-side stand-in, never a device address.
+int noalloc_scratch(uint32_t** out) {
+    static std::mutex lock;
+    static std::vector<uint32_t*> per_device;
+    int device = 0;
+    cudaError_t err = cudaGetDevice(&device);
+    if (err != cudaSuccess) return nz::fail(NZ_ECUDA, std::string("cudaGetDevice: ") + cudaGetErrorString(err));
+    std::lock_guard<std::mutex> hold(lock);
+    if (per_device.size() <= static_cast<size_t>(device)) per_device.resize(device + 1, nullptr);
+    if (!per_device[device]) {
+        uint32_t* ptr = nullptr;
+        err = cudaGetSymbolAddress(reinterpret_cast<void**>(&ptr), g_noalloc_scratch);
+        if (err != cudaSuccess)
+            return nz::fail(NZ_ECUDA, std::string("cudaGetSymbolAddress: ") + cudaGetErrorString(err));
+        err = cudaMemset(ptr, 0, sizeof(g_noalloc_scratch));
+        if (err == cudaSuccess) err = cudaDeviceSynchronize();
+        if (err != cudaSuccess) return nz::fail(NZ_ECUDA, std::string("cudaMemset: ") + cudaGetErrorString(err));
+        per_device[device] = ptr;
+    }
+    *out = per_device[device];
+    return NZ_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -758,6 +789,19 @@ int nz_decode_launch_many(const nz_launch* launches, uint32_t count, void* cuda_
         ++k;
     }
     return NZ_OK;
+}
+
+int nz_decode_launch_noalloc(const nz_launch* launch, void* cuda_stream) {
+    if (!launch) return nz::fail(NZ_EVALUE, "Null launch descriptor.");
+    if (launch->queues > kNoAllocQueues)
+        return nz::fail(NZ_EVALUE, "nz_decode_launch_noalloc takes at most 1024 work queues.");
+    if (launch->n_ctas == 0) return NZ_OK;
+    uint32_t* scratch = nullptr;
+    const int rc = noalloc_scratch(&scratch);
+    if (rc != NZ_OK) return rc;
+    nz_launch l = *launch;
+    l.scratch = reinterpret_cast<uint64_t>(scratch);
+    return nz_decode_launch(&l, cuda_stream);
 }
 
 int nz_decode_launch(const nz_launch* launch, void* cuda_stream) {

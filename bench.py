@@ -8,8 +8,9 @@ N(0, 0.02); default NeuralZipSetup (JS clustering, up to 254 pairs). Data
 are synthetic (seeded); rank r uses seed 1 + r, so N ranks decode N disjoint
 workloads with no collective (weak scaling).
 
-A step decodes every chunk once: a bf16 launch, then one launch mixing the
-fp16 and fp32 groups (each CTA names its element layout). `value`
+A step decodes every chunk once: a bf16 launch, and one launch mixing the
+fp16 and fp32 groups (each CTA names its element layout) enqueued at once on
+a low-priority side stream, as nz_decode_launch_many runs them. `value`
 is decoded bytes of all ranks / the slowest rank's step time, inputs
 resident in HBM (2.2 GB of outputs and 1.4 GB of inputs per rank, larger
 than L2, so no flush is needed). `e2e` times the same decode through the

@@ -530,16 +530,6 @@ std::vector<uint8_t> write_huff0_header(const uint8_t* lengths, uint32_t nsym) {
 
 using nz::Error;
 
-#define NZ_GUARD(...)                                   \
-    try {                                                \
-        __VA_ARGS__;                                            \
-        return NZ_OK;                                    \
-    } catch (const Error& e) {                           \
-        return nz::fail(e.status, e.what());             \
-    } catch (const std::exception& e) {                  \
-        return nz::fail(NZ_ERUNTIME, e.what());          \
-    }
-
 extern "C" {
 
 int nz_export_code_table(const uint8_t* header, size_t header_size, const uint8_t* vocab,

@@ -246,8 +246,9 @@ typedef struct nz_cta {
  * One launch decodes groups of any mix of layouts (each CTA names its
  * own). All arrays are device-resident; `luts` is a device array of device
  * pointers to NZ_LUT_WORDS-word tables. `status` (device int32) receives a
- * nonzero code if a corrupt table made a lane give up (2) or a CTA named an
- * unknown layout (3); it is only written on error. Asynchronous on
+ * nonzero code if a corrupt table made a lane give up (2), a CTA named an
+ * unknown layout (3) or, in a queue launch, a queue index not below
+ * `queues` (4); it is only written on error. Asynchronous on
  * `cuda_stream` (a cudaStream_t, NULL = legacy default stream).
  * warps_per_cta: 4, 8, 16 or 24 (0 = default, 8); 24-warp CTAs fill an SM
  * alone, 8- and 4-warp CTAs run two and three to an SM. */
@@ -261,8 +262,8 @@ typedef struct nz_launch {
     uint64_t status;   /* int32_t* */
     /* uint32_t[queues + 1], zero before the first launch that uses it; the
      * launch's last CTA sets it back to zero. 0: no queues, each CTA
-     * decodes its own range. Launches that share scratch must not overlap
-     * on the GPU. */
+     * decodes its own range (also when queues is 0). Launches that share
+     * scratch must not overlap on the GPU. */
     uint64_t scratch;
     uint32_t queues;
     uint32_t reserved; /* zero */
@@ -275,8 +276,8 @@ int nz_decode_launch(const nz_launch* launch, void* cuda_stream);
  * HBM, or a host path that must not call cudaMalloc because it may
  * synchronize the device. It allocates nothing; the caller still passes
  * every input and output. launch->scratch is ignored and launch->queues
- * must be at most 1024 (NZ_EVALUE otherwise); the CTAs name their queues
- * as for nz_decode_launch. The counters (4 KB per GPU that loads the
+ * must be at most 1024 (NZ_EVALUE otherwise; 0 gives the fixed-range
+ * launch); the CTAs name their queues as for nz_decode_launch. The counters (4 KB per GPU that loads the
  * library, held until the process exits) are looked up and cleared by the
  * first call on each device, which should therefore come before any stream
  * capture; each launch's last CTA sets them back to zero. All calls on

@@ -325,7 +325,6 @@ __device__ __forceinline__ void decode_works(const nz_group* __restrict__ groups
     // (lane 0, one atomic per work), the next claim issued halfway through
     // the current work so that the atomic's round trip is hidden.
     uint32_t w = begin + warp;
-    if (kQueue && !queue) return;  // see nz_tile_decode
     if constexpr (kQueue) {
         uint32_t first = 0;
         if (lane == 0) first = atomicAdd(queue, 1U);
@@ -535,6 +534,7 @@ __device__ __forceinline__ void decode_works(const nz_group* __restrict__ groups
 }
 
 constexpr int32_t kStatusBadLayout = 3;
+constexpr int32_t kStatusBadQueue = 4;
 
 // One launch covers CTAs of every element layout: each CTA stages its
 // decode table and runs the body of its layout (uniform per CTA, so the
@@ -552,8 +552,10 @@ __global__ void __launch_bounds__(NW * 32, ctas_per_sm(NW))
     uint32_t* stage = smem + NZ_LUT_WORDS + (threadIdx.x >> 5) * warp_words(NW);
 
     const nz_cta cta = ctas[blockIdx.x];
-    // A CTA whose queue index is out of range takes its own range.
-    uint32_t* queue = kQueue && cta.queue < queues ? scratch + cta.queue : nullptr;
+    // A queue launch's CTA whose queue index is out of range sets status 4
+    // and decodes nothing (as a CTA with an unknown layout).
+    const bool bad_queue = kQueue && cta.queue >= queues;
+    uint32_t* queue = kQueue && !bad_queue ? scratch + cta.queue : nullptr;
     if (cta.lut != NZ_RAW_LUT) {
         const uint4* src = reinterpret_cast<const uint4*>(luts[cta.lut]);
         uint4* dst = reinterpret_cast<uint4*>(table);
@@ -561,7 +563,7 @@ __global__ void __launch_bounds__(NW * 32, ctas_per_sm(NW))
         for (uint32_t i = threadIdx.x; i < n4; i += NW * 32) dst[i] = __ldg(src + i);
     }
     __syncthreads();
-    switch (cta.layout) {
+    switch (bad_queue ? 0xFFFFU : cta.layout) {
         case NZ_LAYOUT_BF16:
             decode_works<2, true, NW, kQueue>(groups, works, cta.begin, cta.end, table, stage, status, queue);
             break;
@@ -572,7 +574,7 @@ __global__ void __launch_bounds__(NW * 32, ctas_per_sm(NW))
             decode_works<4, true, NW, kQueue>(groups, works, cta.begin, cta.end, table, stage, status, queue);
             break;
         default:
-            if (threadIdx.x == 0 && status) *status = kStatusBadLayout;
+            if (threadIdx.x == 0 && status) *status = bad_queue ? kStatusBadQueue : kStatusBadLayout;
     }
     if constexpr (kQueue) {
         // The launch's last CTA to finish sets the queue counters back to
@@ -619,7 +621,8 @@ cudaError_t launch_kernel(const nz_launch& l, cudaStream_t stream) {
 
 template <int NW>
 cudaError_t launch_one(const nz_launch& l, cudaStream_t stream) {
-    return l.scratch ? launch_kernel<NW, true>(l, stream) : launch_kernel<NW, false>(l, stream);
+    // Queues only with scratch and at least one queue; else fixed ranges.
+    return l.scratch && l.queues ? launch_kernel<NW, true>(l, stream) : launch_kernel<NW, false>(l, stream);
 }
 
 cudaError_t launch_nw(const nz_launch& l, cudaStream_t stream) {

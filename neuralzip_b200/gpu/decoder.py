@@ -308,10 +308,13 @@ class TileDecoder:
 
     @staticmethod
     def check_status(prepared):
-        """Raises if a launch of this batch reported a corrupt decode table."""
+        """Raises if a launch of this batch reported an error: a corrupt
+        decode table (2), an unknown element layout (3) or a work-queue
+        index out of range (4)."""
         code = int(prepared.status.item())
         if code:
-            raise RuntimeError(f"The GPU decoder reported status {code} (corrupt decode table).")
+            what = {2: "corrupt decode table", 3: "unknown element layout", 4: "work-queue index out of range"}
+            raise RuntimeError(f"The GPU decoder reported status {code} ({what.get(code, 'unknown error')}).")
 
 
 _DECODER = TileDecoder()

@@ -262,6 +262,16 @@ def test_c_abi_work_queues_by_hand():
         assert bytes(out.cpu().view(torch.uint8).numpy()) == raw
         assert int(status.item()) == 0
         assert scratch.tolist() == [0, 0]
+    # A CTA naming a queue the launch does not have writes nothing and
+    # reports status 4; the counters still end at zero.
+    out.view(torch.int16).fill_(-1)
+    ctas["queue"] = 7
+    dev[2].copy_(torch.from_numpy(ctas.view(np.uint8).copy()))
+    _native.decode_launch(launch, torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 4
+    assert bool((out.view(torch.int16) == -1).all())
+    assert scratch.tolist() == [0, 0]
 
 
 @pytest.mark.parametrize("work_queues", [False, True])

@@ -12,15 +12,22 @@
 //     prefix scan and no __syncthreads in the decode loop (the reference
 //     decodes every segment twice and scans with two block barriers,
 //     decode.cu:129-175, 207-255);
+//   * the warp copies its tile's bitstream into shared memory (cp.async)
+//     and its lanes refill their bit windows from there (the reference's
+//     threads read their segments from global memory);
 //   * the decode table lives in shared memory (staged once per CTA) and one
 //     8-byte lookup of the 12-bit window yields up to four output bytes (two
-//     pair tokens); codes of 13..56 bits continue through a suffix tree in
-//     the same table
-//     (decode.cu:41-60 reads its table through __ldg, one token per probe);
-//   * decoded bytes are staged per warp, 64 elements per lane at a time, and
-//     merged with the raw lanes through 8-byte loads and 16-byte stores that
-//     are contiguous across the warp (decode.cu:83-100 loads and stores one
-//     element at a time).
+//     pair tokens); codes of 13..31 bits are resolved from canonical limits
+//     in the same table, longer ones through a suffix tree
+//     (decode.cu:41-60 reads its table through __ldg, one token per probe,
+//     and walks long codes bit by bit);
+//   * decoded bytes are staged per warp, 128 elements per lane at a time,
+//     and merged with the raw lanes through 8-byte loads and 16-byte stores
+//     that are contiguous across the warp (decode.cu:83-100 loads and
+//     stores one element at a time);
+//   * one CTA per SM (24 warps); the CTAs of one decode table can share its
+//     tiles through an atomic work queue, so that they finish together
+//     (the reference launches one grid per group layout, sized per group).
 
 #include "nz_b200.h"
 #include "nz_internal.h"

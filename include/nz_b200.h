@@ -304,8 +304,9 @@ int nz_decode_occupancy(uint32_t warps_per_cta, uint32_t* ctas_per_sm);
 int nz_decode_smem_bytes(uint32_t warps_per_cta, uint32_t* bytes);
 /* Words of a tile's bitstream a warp copies into shared memory at
  * warps_per_cta (956, 1964, 1336, 1296 for 24, 16, 8, 4 warps): from the
- * 16-byte boundary at or below the tile's first bit through at least four
- * words past its last one. A larger tile is read from global memory,
+ * 16-byte boundary at or below the tile's first bit through at least 12
+ * words past the word of its last one. A larger tile is read from global
+ * memory,
  * slower. No reference counterpart (decode.cu reads global memory). */
 int nz_decode_tile_words(uint32_t warps_per_cta, uint32_t* words);
 

@@ -421,10 +421,6 @@ __device__ __forceinline__ void decode_works(const nz_group* __restrict__ groups
                 for (int l = 0; l < L::kRawLanes; ++l) prefetch_l2(lanes[l] + tile_base, n);
             }
         }
-        // The tile's bits, from the 16-byte word boundary at or below its
-        // first bit through four words past its last one (the read-ahead),
-        // are copied into the warp's buffer when they fit; inside the stream
-        // and its 16-word zero pad.
         // Byte queue: `qbits` bits (0, 8, 16 or 24) of decoded bytes wait in
         // qa between lookups. A lookup's bytes that do not fit in qa are not
         // kept: when qa fills up it is stored and rebuilt from the entry.
@@ -510,9 +506,17 @@ __device__ __forceinline__ void decode_works(const nz_group* __restrict__ groups
             }
         };
         {
+            // The tile's bits are copied into the warp's buffer when they
+            // fit: from the 16-byte boundary at or below the first bit
+            // through 12 to 15 words past the word of the last bit, inside
+            // the stream's zero pad of at least 16 words. Lanes read past
+            // their last bit: the window's read-ahead (3 words), and, for a
+            // ragged last sub-stream, up to 3 lookups of bits that are not
+            // its own (at most 3 x 56 bits) until its staged word is full;
+            // at most 9 words in all, so every read stays in the copy.
             const uint32_t* gbits = reinterpret_cast<const uint32_t*>(g.bits);
             const uint32_t wa = (bit0 >> 5) & ~3U;
-            const uint32_t wb = (((bit0 + tile_bits) >> 5) + 8U) & ~3U;
+            const uint32_t wb = (((bit0 + tile_bits) >> 5) + 16U) & ~3U;
             if (wb - wa <= kBitBufWords) {
                 uint32_t* buf = stage + kStageWordsPerWarp;
                 const uint32_t sbuf = static_cast<uint32_t>(__cvta_generic_to_shared(buf));

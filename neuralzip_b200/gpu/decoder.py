@@ -84,13 +84,13 @@ class DeviceGroup:
 
 def tile_copy_words(tile_offsets, bit_length):
     """Largest shared-memory copy of one tile's bitstream, in words: from
-    the 16-byte boundary at or below its first bit through the word four to
-    seven past its last bit (what the kernel copies)."""
+    the 16-byte boundary at or below its first bit through the word 12 to
+    15 past the word of its last bit (what the kernel copies)."""
     starts = np.asarray(tile_offsets, dtype=np.int64)
     if not len(starts):
         return 0
     ends = np.append(starts[1:], int(bit_length))
-    return int(((((ends >> 5) + 8) & ~3) - ((starts >> 5) & ~3)).max())
+    return int(((((ends >> 5) + 16) & ~3) - ((starts >> 5) & ~3)).max())
 
 
 @dataclass(frozen=True)

@@ -240,8 +240,9 @@ def test_tile_copy_words_matches_kernel_bounds():
     from neuralzip_b200.gpu.decoder import tile_copy_words
 
     # Tiles at bits [0, 100), [100, 5000), [5000, 5001): the copy runs from
-    # the 16-byte boundary at or below the first bit to 4..7 words past the
-    # last one.
-    assert tile_copy_words([0, 100, 5000], 5001) == max(((100 >> 5) + 8) & ~3, (((5000 >> 5) + 8) & ~3) - ((100 >> 5) & ~3),
-                                                         (((5001 >> 5) + 8) & ~3) - ((5000 >> 5) & ~3))
+    # the 16-byte boundary at or below the first bit to 12..15 words past
+    # the word of the last one.
+    assert tile_copy_words([0, 100, 5000], 5001) == max(((100 >> 5) + 16) & ~3,
+                                                         (((5000 >> 5) + 16) & ~3) - ((100 >> 5) & ~3),
+                                                         (((5001 >> 5) + 16) & ~3) - ((5000 >> 5) & ~3))
     assert tile_copy_words([], 0) == 0

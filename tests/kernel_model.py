@@ -117,6 +117,13 @@ def decode_group(lut, bits, lens, tile_off, numel, lut_words=None):
                     qbits = qn & 31
                 if want:
                     out[first + done:first + done + want] = np.frombuffer(bytes(staged), dtype=np.uint8)[:want]
+            # Every word the lane read lies in the tile's shared-memory copy:
+            # from the 16-byte boundary at or below the tile's first bit
+            # through 12..15 words past the word of its last bit.
+            start, end = int(tile_off[tile]), int(tile_off[tile]) + sum(lens_t)
+            wa, wb = (start >> 5) & ~3, ((end >> 5) + 16) & ~3
+            assert wa <= (int(tile_off[tile]) + sum(lens_t[:lane])) >> 5 and win.ptr <= wb, \
+                f"lane {lane} of tile {tile} read word {win.ptr - 1} outside the copy [{wa}, {wb})"
     return out
 
 

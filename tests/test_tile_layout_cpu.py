@@ -133,3 +133,54 @@ def test_merge_arithmetic_model_restores_elements(dtype):
             words = KM.merge_fp32_words(word(0, i), word(1, i), word(2, i), word(3, i))
         got = b"".join(w.to_bytes(4, "little") for w in words)
         assert got == raw[4 * es * i:4 * es * (i + 1)].tobytes(), i
+
+
+@pytest.mark.parametrize("seed", [0, 1, 2, 3])
+def test_random_long_code_books_decode_through_canonical_tables(seed):
+    """Random skewed histograms over 256 bytes and 254 pairs give codes of
+    up to 31 bits; they decode through the canonical limit/offset/leaf
+    tables (no suffix tree staged), identically in the kernel model and the
+    oracle's bit-by-bit reader."""
+    rng = np.random.default_rng(100 + seed)
+    counts = (rng.pareto(0.6 + 0.1 * seed, size=510) * 10).astype(np.int64) + 1
+    counts[rng.integers(0, 510, size=8)] = 1 << 24  # a few dominant tokens push the rest long
+    lengths = H.huffman_lengths_heap(counts)
+    longest = max(lengths)
+    if not 13 <= longest <= 31:
+        pytest.skip(f"longest code {longest} is outside the canonical range")
+    vocab = rng.choice(65536, size=254, replace=False).astype("<u2").tobytes()
+    book = GPUCodebook(tuple(lengths), tuple(int(v) for v in O.mixed_codes(lengths)), vocab)
+    assert book.table_words == _native.LUT_TREE
+    spec = DTYPES[torch.bfloat16]
+    symbols = rng.integers(0, 256, size=3 * 8192 + 77, dtype=np.uint8)
+    _roundtrip(H.lanes_with(symbols, spec), spec, book)
+
+
+def test_long_codes_in_any_order_within_a_length_use_the_limit_tables():
+    """The limit tables need only that each length's codes are consecutive
+    values and that longer codes have larger left-justified values: the
+    symbols of one length may take them in any order."""
+    lengths = H.segment_lengths(20)
+    canonical = [int(v) for v in O.mixed_codes(lengths)]
+    values = list(canonical)
+    for length in set(lengths):
+        idx = [i for i, n in enumerate(lengths) if n == length]
+        for i, j in zip(idx, reversed(idx)):
+            values[i] = canonical[j]
+    book = GPUCodebook(tuple(lengths), tuple(values), H.VOCAB)
+    assert book.table_words == _native.LUT_TREE
+    spec = DTYPES[torch.bfloat16]
+    _roundtrip(H.lanes_with(H.segment_symbols(), spec), spec, book)
+
+
+def test_non_canonical_long_codes_use_the_suffix_tree():
+    """Codes with every bit flipped (still a complete prefix code, but the
+    longest codes now have the smallest values) cannot use the limit
+    tables: the kernel walks the suffix tree instead, with the same
+    result."""
+    lengths = H.segment_lengths(20)
+    values = [(1 << n) - 1 - int(v) for n, v in zip(lengths, O.mixed_codes(lengths))]
+    book = GPUCodebook(tuple(lengths), tuple(values), H.VOCAB)
+    assert book.table_words > _native.LUT_TREE
+    spec = DTYPES[torch.bfloat16]
+    _roundtrip(H.lanes_with(H.segment_symbols(), spec), spec, book)

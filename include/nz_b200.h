@@ -245,10 +245,13 @@ typedef struct nz_cta {
  * the kernel launch of decode_batched (neuralzip/gpu/cuda/decode.cu:323).
  * One launch decodes groups of any mix of layouts (each CTA names its
  * own). All arrays are device-resident; `luts` is a device array of device
- * pointers to NZ_LUT_WORDS-word tables. `status` (device int32) receives a
+ * pointers to NZ_LUT_WORDS-word tables, each 16-byte aligned (a CTA
+ * stages its table with one bulk copy). `status` (device int32) receives a
  * nonzero code if a corrupt table made a lane give up (2), a CTA named an
  * unknown layout (3) or, in a queue launch, a queue index not below
- * `queues` (4); it is only written on error. Asynchronous on
+ * `queues` (4), or if a table copy did not complete within the kernel's
+ * bounded wait (5; that CTA decodes nothing); it is only written on
+ * error. Asynchronous on
  * `cuda_stream` (a cudaStream_t, NULL = legacy default stream).
  * warps_per_cta: 4, 8, 16 or 24 (0 = default, 8); 24-warp CTAs fill an SM
  * alone, 8- and 4-warp CTAs run two and three to an SM. */
@@ -303,7 +306,7 @@ int nz_decode_occupancy(uint32_t warps_per_cta, uint32_t* ctas_per_sm);
 /* Dynamic shared memory one CTA of nz_decode_launch uses. */
 int nz_decode_smem_bytes(uint32_t warps_per_cta, uint32_t* bytes);
 /* Words of a tile's bitstream a warp copies into shared memory at
- * warps_per_cta (956, 1964, 1336, 1296 for 24, 16, 8, 4 warps): from the
+ * warps_per_cta (956, 1960, 1332, 1292 for 24, 16, 8, 4 warps): from the
  * 16-byte boundary at or below the tile's first bit through at least 12
  * words past the word of its last one. A larger tile is read from global
  * memory,

@@ -44,28 +44,30 @@ constexpr uint32_t kRoundElems = 128;                      // per lane per stagi
 constexpr uint32_t kRounds = NZ_LANE_ELEMS / kRoundElems;  // 2
 constexpr uint32_t kStageStride = kRoundElems / 4 + 1;     // words per staged row (odd: no conflicts)
 constexpr uint32_t kStageWordsPerWarp = NZ_TILE_LANES * kStageStride;
-// A CTA's shared memory holds the decode table and, per warp, the staging
-// rows plus a copy of the warp's current tile bitstream. CTAs of 24 and 16
-// warps run one to an SM, of 8 and 4 warps two and three; each width gets
-// the largest bitstream copy (a multiple of four words) that keeps that
-// many CTAs resident: 956, 1964, 1336 and 1296 words.
+// A CTA's shared memory holds the decode table, per warp the staging rows
+// plus a copy of the warp's current tile bitstream, and the mbarrier the
+// table copy completes on (kBarWords). CTAs of 24 and 16 warps run one to
+// an SM, of 8 and 4 warps two and three; each width gets the largest
+// bitstream copy (a multiple of four words) that keeps that many CTAs
+// resident: 956, 1960, 1332 and 1292 words.
 constexpr uint32_t kSmemPerSm = 233472;     // 228 KB
 constexpr uint32_t kSmemPerBlock = 232448;  // 227 KB opt-in limit
 constexpr uint32_t kSmemReserved = 1024;    // per resident CTA
+constexpr uint32_t kBarWords = 4;           // one 8-byte mbarrier, kept 16-byte aligned
 __host__ __device__ constexpr uint32_t ctas_per_sm(uint32_t nw) { return nw >= 16 ? 1U : (nw >= 8 ? 2U : 3U); }
 __host__ __device__ constexpr uint32_t bit_buf_words(uint32_t nw) {
     return (((kSmemPerSm / ctas_per_sm(nw) - kSmemReserved < kSmemPerBlock
                   ? kSmemPerSm / ctas_per_sm(nw) - kSmemReserved
                   : kSmemPerBlock) /
                  4U -
-             NZ_LUT_WORDS) /
+             NZ_LUT_WORDS - kBarWords) /
                 nw -
             kStageWordsPerWarp) &
            ~3U;
 }
 __host__ __device__ constexpr uint32_t warp_words(uint32_t nw) { return kStageWordsPerWarp + bit_buf_words(nw); }
-static_assert(bit_buf_words(24) == 956 && bit_buf_words(16) == 1964 && bit_buf_words(8) == 1336 &&
-                  bit_buf_words(4) == 1296,
+static_assert(bit_buf_words(24) == 956 && bit_buf_words(16) == 1960 && bit_buf_words(8) == 1332 &&
+                  bit_buf_words(4) == 1292,
               "bitstream copy per warp");
 constexpr uint32_t kLanesPerRow = kRoundElems / 8;          // merge: 8 elements per lane
 constexpr uint32_t kRowsPerPass = 32 / kLanesPerRow;
@@ -73,6 +75,41 @@ constexpr uint32_t kMergePasses = NZ_TILE_LANES / kRowsPerPass;
 constexpr uint32_t kTreeMask = NZ_TREE_MAX_NODES - 1;
 constexpr uint32_t kMaxTreeDepth = NZ_MAX_CODE_BITS - NZ_LUT_BITS;
 constexpr int32_t kStatusCorruptTable = 2;
+
+// Polls of a bounded mbarrier wait: far beyond any copy's latency (each
+// poll may also suspend the thread for a while), yet finite.
+constexpr uint32_t kMaxBarrierPolls = 1U << 22;
+constexpr int32_t kStatusCopyTimeout = 5;
+
+__device__ __forceinline__ void mbar_init(uint32_t bar) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+// One thread: copies `bytes` (a multiple of 16, both addresses 16-byte
+// aligned) from this GPU's global memory into this CTA's shared memory with
+// the bulk-copy (TMA) engine; the copy completes on `bar`. No multicast.
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+                 "l"(src), "r"(bytes), "r"(bar)
+                 : "memory");
+}
+
+// Waits for phase `parity` of `bar`; false after kMaxBarrierPolls polls.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+    for (uint32_t i = 0; i < kMaxBarrierPolls; ++i) {
+        uint32_t done;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(done)
+            : "r"(bar), "r"(parity)
+            : "memory");
+        if (done) return true;
+    }
+    return false;
+}
 
 // Streaming 8-byte load of a raw lane: read once, kept out of L1.
 __device__ __forceinline__ uint2 ldg_u2(const void* p) {
@@ -567,14 +604,28 @@ __global__ void __launch_bounds__(NW * 32, ctas_per_sm(NW))
     // and decodes nothing (as a CTA with an unknown layout).
     const bool bad_queue = kQueue && cta.queue >= queues;
     uint32_t* queue = kQueue && !bad_queue ? scratch + cta.queue : nullptr;
+    // The decode table (its leading table words, rounded up to 16 bytes)
+    // arrives by one bulk copy issued by thread 0. A copy that does not
+    // complete within the bounded wait sets status 5, and after a second
+    // bounded wait for it the CTA decodes nothing.
+    bool table_ok = true;
     if (cta.lut != NZ_RAW_LUT) {
-        const uint4* src = reinterpret_cast<const uint4*>(luts[cta.lut]);
-        uint4* dst = reinterpret_cast<uint4*>(table);
-        const uint32_t n4 = (min(static_cast<uint32_t>(cta.lut_words), NZ_LUT_WORDS) + 3U) / 4U;
-        for (uint32_t i = threadIdx.x; i < n4; i += NW * 32) dst[i] = __ldg(src + i);
+        const uint32_t bar = static_cast<uint32_t>(__cvta_generic_to_shared(smem + NZ_LUT_WORDS + NW * warp_words(NW)));
+        if (threadIdx.x == 0) mbar_init(bar);
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            const uint32_t n4 = (min(static_cast<uint32_t>(cta.lut_words), NZ_LUT_WORDS) + 3U) / 4U;
+            bulk_load(static_cast<uint32_t>(__cvta_generic_to_shared(table)),
+                      reinterpret_cast<const void*>(luts[cta.lut]), n4 * 16U, bar);
+        }
+        table_ok = mbar_wait(bar, 0U);
+        if (!table_ok) {
+            if (threadIdx.x == 0 && status) *status = kStatusCopyTimeout;
+            mbar_wait(bar, 0U);
+        }
     }
     __syncthreads();
-    switch (bad_queue ? 0xFFFFU : cta.layout) {
+    switch (bad_queue || !table_ok ? 0xFFFFU : cta.layout) {
         case NZ_LAYOUT_BF16:
             decode_works<2, true, NW, kQueue>(groups, works, cta.begin, cta.end, table, stage, status, queue);
             break;
@@ -585,7 +636,7 @@ __global__ void __launch_bounds__(NW * 32, ctas_per_sm(NW))
             decode_works<4, true, NW, kQueue>(groups, works, cta.begin, cta.end, table, stage, status, queue);
             break;
         default:
-            if (threadIdx.x == 0 && status) *status = bad_queue ? kStatusBadQueue : kStatusBadLayout;
+            if (threadIdx.x == 0 && status && table_ok) *status = bad_queue ? kStatusBadQueue : kStatusBadLayout;
     }
     if constexpr (kQueue) {
         // The launch's last CTA to finish sets the queue counters back to
@@ -604,19 +655,28 @@ __global__ void __launch_bounds__(NW * 32, ctas_per_sm(NW))
 
 template <int NW>
 constexpr size_t smem_bytes() {
-    return (NZ_LUT_WORDS + NW * warp_words(NW)) * sizeof(uint32_t);
+    return (NZ_LUT_WORDS + NW * warp_words(NW) + kBarWords) * sizeof(uint32_t);
 }
 
-// Opts the instantiation into its dynamic shared memory (once per process).
+// Opts the instantiation into its dynamic shared memory on the current
+// device. The attribute belongs to the device's context, so it is set once
+// per device (a process may launch on several GPUs).
 template <int NW, bool kQueue>
 cudaError_t ensure_smem_attribute() {
-    static std::once_flag once;
-    static cudaError_t err = cudaSuccess;
-    std::call_once(once, [&]() {
+    static std::mutex lock;
+    static std::vector<char> done;
+    int device = 0;
+    cudaError_t err = cudaGetDevice(&device);
+    if (err != cudaSuccess) return err;
+    std::lock_guard<std::mutex> hold(lock);
+    if (done.size() <= static_cast<size_t>(device)) done.resize(device + 1, 0);
+    if (!done[device]) {
         err = cudaFuncSetAttribute(nz_tile_decode<NW, kQueue>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    static_cast<int>(smem_bytes<NW>()));
-    });
-    return err;
+        if (err != cudaSuccess) return err;
+        done[device] = 1;
+    }
+    return cudaSuccess;
 }
 
 template <int NW, bool kQueue>
@@ -735,7 +795,7 @@ extern "C" {
 int nz_decode_smem_bytes(uint32_t warps_per_cta, uint32_t* bytes) {
     if (!bytes) return nz::fail(NZ_EVALUE, "Null output.");
     const uint32_t nw = warps_per_cta == 0 ? 8U : warps_per_cta;
-    *bytes = (NZ_LUT_WORDS + nw * warp_words(nw)) * static_cast<uint32_t>(sizeof(uint32_t));
+    *bytes = (NZ_LUT_WORDS + nw * warp_words(nw) + kBarWords) * static_cast<uint32_t>(sizeof(uint32_t));
     return NZ_OK;
 }
 

@@ -309,11 +309,12 @@ class TileDecoder:
     @staticmethod
     def check_status(prepared):
         """Raises if a launch of this batch reported an error: a corrupt
-        decode table (2), an unknown element layout (3) or a work-queue
-        index out of range (4)."""
+        decode table (2), an unknown element layout (3), a work-queue index
+        out of range (4) or a decode-table copy that did not complete (5)."""
         code = int(prepared.status.item())
         if code:
-            what = {2: "corrupt decode table", 3: "unknown element layout", 4: "work-queue index out of range"}
+            what = {2: "corrupt decode table", 3: "unknown element layout", 4: "work-queue index out of range",
+                    5: "decode-table copy did not complete"}
             raise RuntimeError(f"The GPU decoder reported status {code} ({what.get(code, 'unknown error')}).")
 
 

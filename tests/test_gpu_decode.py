@@ -388,3 +388,25 @@ def test_config1_single_tensor_singleton():
     got = dict(runtime.materialized_weights())["w"]
     assert torch.equal(got.reshape(-1).view(torch.uint8), named["w"].reshape(-1).view(torch.uint8))
     runtime.check_status()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_same_process_decodes_on_two_devices():
+    """The kernel's shared-memory opt-in belongs to each device's context:
+    one process decodes the same tensors on cuda:0 and on cuda:1, with the
+    24-warp (232 KB) CTAs on both."""
+    from neuralzip_b200.gpu.inference import NeuralZipRuntime, export_tensors_for_gpu
+    from neuralzip_b200.setup import NeuralZipSetup
+
+    g = torch.Generator().manual_seed(3)
+    named = {f"w{i}": (torch.randn(1024, 8192, generator=g) * 0.02).to(torch.bfloat16) for i in range(20)}
+    export = export_tensors_for_gpu(named, NeuralZipSetup().build(named))
+    for device in ("cuda:0", "cuda:1"):
+        runtime = NeuralZipRuntime(None, export, device)
+        batch = runtime._prepared_batches[export.block_order[0]][0]
+        assert batch.warps_per_cta == 24
+        runtime.workspaces[torch.bfloat16].view(torch.uint8).fill_(0xA5)
+        got = dict(runtime.materialized_weights())
+        for name, tensor in named.items():
+            assert torch.equal(got[name].reshape(-1).view(torch.uint8), tensor.reshape(-1).view(torch.uint8))
+        runtime.check_status()

@@ -590,6 +590,18 @@ int nz_huff0_build(const uint64_t* counts, uint32_t max_bits, uint8_t* header_ou
         if (max_bits < 1 || max_bits > 12) throw Error(NZ_EVALUE, "max_bits must be in [1, 12].");
         uint8_t lengths[256];
         nz::huffman_lengths(counts, 256, max_bits, lengths);
+        // A 1-bit code beside 12-bit codes has weight 12. zstd's decoder
+        // reads that weight from 4-bit direct weights but rejects it in
+        // FSE-coded weights (measured with libzstd 1.5.5; its weight
+        // decoder takes weights up to 11 there), so such a table is built
+        // with 11 bits instead and stays readable by zstd's Huff0.
+        uint32_t shortest = 255, longest = 0;
+        for (uint32_t s = 0; s < 256; ++s)
+            if (lengths[s]) {
+                shortest = std::min<uint32_t>(shortest, lengths[s]);
+                longest = std::max<uint32_t>(longest, lengths[s]);
+            }
+        if (longest == 12 && shortest == 1) nz::huffman_lengths(counts, 256, 11, lengths);
         const std::vector<uint8_t> header = nz::write_huff0_header(lengths, 256);
         if (header.size() > cap) throw Error(NZ_EVALUE, "Header buffer is too small.");
         std::memcpy(header_out, header.data(), header.size());

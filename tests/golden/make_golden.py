@@ -3,8 +3,10 @@
 Run in a checkout where the reference sources exist (oracle/Makefile builds
 oracle/_ref/libnzref.so from them): ``python tests/golden/make_golden.py``.
 Every array comes from the reference's native functions compiled unchanged
-(make_mixed_table, encode_gpu_layout, encode_mixed_block_into); the inputs
-are seeded and restated here. The fixtures let the CPU tests pin the oracle
+(make_mixed_table, encode_gpu_layout, encode_mixed_block_into), except the
+singleton table, whose header the system zstd library writes (zstd's Huff0
+is the reference's singleton codec and is not in its tree); the inputs are
+seeded and restated here. The fixtures let the CPU tests pin the oracle
 and the product without the reference tree.
 """
 
@@ -49,15 +51,21 @@ def main():
     arrays["gauss_vocab"] = np.frombuffer(vocab, dtype=np.uint8)
     arrays["gauss_codes"] = O.ref_mixed_codes_native(lengths, vocab)
     cases["gauss_bf16"] = ("gauss", torch.bfloat16, raw)
-    # A singleton table (lengths/values in the Huff0 convention: longest
-    # codes first) exercises the 4-bit gap path.
-    counts = np.bincount(sel, minlength=256) + 1
-    from neuralzip_b200 import _native
+    # A singleton table exercises the 4-bit gap path. Its header is the
+    # Huffman tree description the system zstd library writes for these
+    # bytes (a literals-only frame); the lengths and codes are read from it
+    # by the RFC 8878 restatement in oracle/rfc8878.py, not by the product.
+    import zstd_frames as Z
+    from oracle import rfc8878 as R
 
-    header, _ = _native.huff0_build(counts, 12)
-    s_lengths, s_values, _, _ = _native.huff0_read(header)
-    arrays["single_lengths"] = np.frombuffer(s_lengths, dtype=np.uint8)
-    arrays["single_codes"] = np.asarray(s_values, dtype=np.uint64)
+    zstd = Z.library()
+    if zstd is None:
+        raise SystemExit("libzstd is needed for the singleton table.")
+    (_kind, block), = Z.frame_blocks(Z.literals_frame(zstd, bytes(sel)))
+    header = Z.literals_section(block)[2]
+    s_lengths, _used = R.tree_description(header)
+    arrays["single_lengths"] = np.asarray(s_lengths, dtype=np.uint8)
+    arrays["single_codes"] = np.asarray(R.canonical_codes(s_lengths), dtype=np.uint64)
     arrays["single_header"] = np.frombuffer(header, dtype=np.uint8)
     cases["single_bf16"] = ("single", torch.bfloat16, raw)
     for case, (book, dtype, data) in cases.items():

@@ -10,10 +10,11 @@
 // Unit u decodes into slot u % depth. With overlap, the hook of a unit's
 // first block waits for the unit's side-stream decode (or decodes it on the
 // compute stream if none is pending) and then starts the side-stream decode
-// of the next units whose slots are free: a slot is free once its previous
-// reader has been enqueued on the compute stream, which a "free" event
-// recorded on the compute stream at the current hook covers. All ordering
-// between the two streams is by CUDA events; nothing here blocks the host.
+// of the next units of the same forward whose slots are free: a slot is
+// free once its previous reader has been enqueued on the compute stream,
+// which a "free" event recorded on the compute stream at the current hook
+// covers. All ordering between the two streams is by CUDA events; nothing
+// here blocks the host.
 
 #include "nz_b200.h"
 #include "nz_internal.h"
@@ -67,11 +68,16 @@ int decode_unit(nz_schedule& s, uint32_t unit, cudaStream_t stream) {
     return NZ_OK;
 }
 
+// Starts the side-stream decode of the units after `unit` in this forward
+// (never past the last unit: the next forward's first unit is decoded by
+// its own hook, so a forward never relies on workspace contents written
+// during the previous one, as the reference decodes each block right
+// before it runs).
 int prefetch(nz_schedule& s, uint32_t unit, cudaStream_t compute) {
     const uint32_t n = s.n_units;
     bool freed = false;
-    for (uint32_t d = 1; d < s.depth && d < n; ++d) {
-        const uint32_t next = (unit + d) % n;
+    for (uint32_t d = 1; d < s.depth && unit + d < n; ++d) {
+        const uint32_t next = unit + d;
         if (s.pending[next]) continue;
         // The slot's previous reader must lie before this unit in the
         // enqueue order; one in [unit, next) has not run yet.

@@ -520,8 +520,10 @@ class NeuralZipRuntime:
 
     With ``overlap`` (the default when there are two or more units) every
     dtype gets ``prefetch_depth`` slots (2 = ping-pong): unit k decodes into
-    slot k % depth, and while unit k runs, units k + 1 .. k + depth - 1 are
-    already being decoded on a side stream. The two streams are ordered with
+    slot k % depth, and while unit k runs, units k + 1 .. k + depth - 1 of
+    the same forward are already being decoded on a side stream (the first
+    unit of a forward is decoded by its own hook, so no forward depends on
+    workspace contents left by the previous one). The two streams are ordered with
     CUDA events only: the compute stream waits for "unit k decoded" before
     unit k runs, and the side stream waits for "everything before unit k
     enqueued" before it reuses a slot, which covers the slot's previous

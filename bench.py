@@ -550,27 +550,27 @@ def cpu_sample(named, setup, max_chunks):
     for name, tensor in named.items():
         if tensor.dtype != torch.bfloat16:
             continue
-        modes = comp._transfer_chunk_modes[comp._transfer_plan_key(name, tensor, 1)]
+        modes = comp.chunk_modes(name, tensor)
         raw = tensor.reshape(-1).view(torch.uint8).numpy()
         for c, mode in enumerate(modes):
-            if mode["kind"] != "mixed_huffman" or len(chunks) >= max_chunks:
+            if mode.kind != "mixed_huffman" or len(chunks) >= max_chunks:
                 continue
             part = raw[c * 2 * CHUNK_ELEMS_BF16:(c + 1) * 2 * CHUNK_ELEMS_BF16]
             lanes = O.split(part, spec)
-            payload = books[mode["codebook_id"]]
+            payload = books[mode.codebook_id]
             lengths = bytes(payload.codebook[4:])
             frame = np.frombuffer(O.ref_mixed_encode_native(lanes[1], lengths, bytes(payload.vocab)), dtype=np.uint8)
-            if mode["codebook_id"] not in decodebooks:
-                decodebooks[mode["codebook_id"]] = O.RefDecodebook(lengths, bytes(payload.vocab))
+            if mode.codebook_id not in decodebooks:
+                decodebooks[mode.codebook_id] = O.RefDecodebook(lengths, bytes(payload.vocab))
             out = np.empty(len(part), dtype=np.uint8)
             job = O.RefChunk()
             job.payload, job.payload_size = frame.ctypes.data, len(frame)
-            job.book = decodebooks[mode["codebook_id"]].handle
+            job.book = decodebooks[mode.codebook_id].handle
             job.lanes[0] = lanes[0].ctypes.data
             job.out, job.numel, job.elem_size, job.reorder, job.stream_id = out.ctypes.data, len(lanes[0]), 2, 1, 1
             chunks.append(job)
             keep.append((frame, lanes, out, part))
-            chunk_books.append((mode["codebook_id"], lengths, bytes(payload.vocab)))
+            chunk_books.append((mode.codebook_id, lengths, bytes(payload.vocab)))
     return chunks, keep, decodebooks, chunk_books
 
 

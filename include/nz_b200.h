@@ -183,6 +183,19 @@ int nz_count_tokens(const uint8_t* data, uint64_t size, const uint8_t* vocab,
  * per-chunk distributions setup clusters (neuralzip/setup.py:91-141). */
 int nz_exponent_histograms(const uint8_t* raw, uint64_t numel, const nz_dtype* dt,
                            uint64_t step, uint64_t* histograms);
+/* Setup-time clustering of chunk exponent distributions (restates the
+ * rule of neuralzip/setup.py:91-141): chunk i (in checkpoint order, a
+ * normalized `bins`-bin distribution of weight weights[i]) joins the
+ * nearest cluster of its class by base-2 Jensen-Shannon distance (ties: the
+ * earliest) when that distance is <= threshold or forced[i] is set, else it
+ * opens a cluster; share = 0 opens one cluster per chunk. Centroids are
+ * weight-averaged and updated after each assignment. Writes assign[count],
+ * the centroids (cap_clusters x bins) and the cluster count. */
+int nz_cluster_chunks(const double* distributions, const double* weights,
+                      const int32_t* classes, const uint8_t* forced,
+                      uint64_t count, uint32_t bins, double threshold,
+                      int32_t share, uint32_t* assign, double* centroids,
+                      uint64_t cap_clusters, uint64_t* n_clusters);
 /* Mixed frame (mixed_huffman.h:127-178). *written = 0 when the frame does
  * not fit `cap`; out may be NULL to measure only. */
 int nz_mixed_encode(const nz_codebook* codebook, const uint8_t* data,
@@ -198,6 +211,38 @@ int nz_huff0_encode(const nz_codebook* codebook, const uint8_t* data,
 /* Replaces HUF_decompress4X_usingDTable (codebooks.h:156-206). */
 int nz_huff0_decode(const nz_codebook* codebook, const uint8_t* block,
                     uint64_t size, uint8_t* out, uint64_t count);
+
+/* Storage v2 decode on the host cores. Replaces the reference's CPU decode
+ * queue, decompress_mixed_streams_many (neuralzip/native/decode_queue.h:
+ * 1-113: per chunk, decode each byte lane, then restore_mixed_stream_chunk,
+ * common.h:198-257, merges the lanes and undoes the sign/exponent reorder)
+ * and its worker pool (common.h:134-185). One piece is one source chunk of
+ * one tensor: `count` elements whose byte lanes are `lanes[0 ..
+ * dt.elem_size)` in lane order, each raw (payload_size == count), a Huff0
+ * 4-stream block (count <= 128 KiB) or a mixed frame, decoded with its
+ * codebook (NULL for raw). The piece's element bytes are written to `out`.
+ * Pieces run on `threads` workers (0: the host cores, at most 16, as the
+ * reference's pool). A corrupt or inconsistent piece makes the call fail
+ * with the message of the lowest failing piece; other pieces may have been
+ * written. */
+#define NZ_CHUNK_RAW 0u
+#define NZ_CHUNK_HUFF0 1u
+#define NZ_CHUNK_MIXED 2u
+typedef struct nz_storage_lane {
+    const uint8_t* payload;
+    uint64_t payload_size;
+    const nz_codebook* codebook;
+    uint32_t mode;       /* NZ_CHUNK_* */
+    uint32_t reserved;   /* zero */
+} nz_storage_lane;
+typedef struct nz_storage_piece {
+    const nz_storage_lane* lanes;
+    uint8_t* out;
+    uint64_t count;
+    nz_dtype dt;         /* elem_size, reorder, mant_bits, exp_bits (stream_id unused) */
+    uint32_t reserved;   /* zero */
+} nz_storage_piece;
+int nz_storage_decode(const nz_storage_piece* pieces, uint64_t count, int32_t threads);
 
 /* ---- device: decode --------------------------------------------------- */
 

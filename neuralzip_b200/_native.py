@@ -75,12 +75,21 @@ WORK_DTYPE = np.dtype([("group", "<u4"), ("tile", "<u4")])
 CTA_DTYPE = np.dtype([("lut", "<u4"), ("begin", "<u4"), ("end", "<u4"), ("lut_words", "<u2"), ("layout", "<u2"),
                       ("queue", "<u4"), ("reserved", "<u4")])
 assert GROUP_DTYPE.itemsize == 72 and WORK_DTYPE.itemsize == 8 and CTA_DTYPE.itemsize == 24
+# Host storage-decode records (nz_storage_lane, nz_storage_piece).
+CHUNK_RAW, CHUNK_HUFF0, CHUNK_MIXED = 0, 1, 2
+CHUNK_MODES = {"raw": CHUNK_RAW, "shared_huff0": CHUNK_HUFF0, "mixed_huffman": CHUNK_MIXED}
+STORAGE_LANE_DTYPE = np.dtype([("payload", "<u8"), ("payload_size", "<u8"), ("codebook", "<u8"), ("mode", "<u4"),
+                               ("reserved", "<u4")])
+STORAGE_PIECE_DTYPE = np.dtype([("lanes", "<u8"), ("out", "<u8"), ("count", "<u8"), ("elem_size", "<u4"),
+                                ("reorder", "<u4"), ("mant_bits", "<u4"), ("exp_bits", "<u4"),
+                                ("stream_id", "<u4"), ("reserved", "<u4")])
+assert STORAGE_LANE_DTYPE.itemsize == 32 and STORAGE_PIECE_DTYPE.itemsize == 48
 
 EXPORTS = (
     "nz_export_code_table", "nz_codebook_create", "nz_codebook_destroy", "nz_codebook_info",
     "nz_codebook_lut", "nz_codebook_table_words", "nz_huff0_build", "nz_huff0_read", "nz_pack_bound", "nz_pack_chunk",
     "nz_pack_many", "nz_split_lanes", "nz_exponent_histograms", "nz_count_tokens", "nz_mixed_encode", "nz_mixed_decode",
-    "nz_huff0_encode", "nz_huff0_decode", "nz_decode_launch", "nz_decode_launch_noalloc", "nz_decode_launch_many", "nz_decode_occupancy", "nz_decode_smem_bytes",
+    "nz_huff0_encode", "nz_huff0_decode", "nz_storage_decode", "nz_cluster_chunks", "nz_decode_launch", "nz_decode_launch_noalloc", "nz_decode_launch_many", "nz_decode_occupancy", "nz_decode_smem_bytes",
     "nz_decode_tile_words",
     "nz_schedule_create", "nz_schedule_destroy", "nz_schedule_enter", "nz_schedule_decode_unit",
     "nz_schedule_drain", "nz_schedule_mark", "nz_last_error",
@@ -137,6 +146,9 @@ def _declare(lib):
         "nz_mixed_decode": [c.c_void_p, c.c_void_p, c.c_uint64, c.c_void_p, c.c_uint64],
         "nz_huff0_encode": [c.c_void_p, c.c_void_p, c.c_uint64, c.c_void_p, c.c_uint64, u64p],
         "nz_huff0_decode": [c.c_void_p, c.c_void_p, c.c_uint64, c.c_void_p, c.c_uint64],
+        "nz_storage_decode": [c.c_void_p, c.c_uint64, c.c_int32],
+        "nz_cluster_chunks": [c.c_void_p, c.c_void_p, c.c_void_p, c.c_void_p, c.c_uint64, c.c_uint32, c.c_double,
+                              c.c_int32, c.c_void_p, c.c_void_p, c.c_uint64, u64p],
         "nz_decode_launch": [c.POINTER(Launch), c.c_void_p],
         "nz_decode_launch_noalloc": [c.POINTER(Launch), c.c_void_p],
         "nz_decode_occupancy": [c.c_uint32, u32p],
@@ -374,6 +386,32 @@ def huff0_decode(codebook, block, count, out=None):
     out = np.empty(count, dtype=np.uint8) if out is None else out
     check(lib.nz_huff0_decode(codebook.handle, _ptr(block), len(block), _ptr(out), int(count)))
     return out
+
+
+def cluster_chunks(distributions, weights, classes, forced, threshold, share=True):
+    """(assignment per chunk, centroids) of nz_cluster_chunks."""
+    lib = load()
+    distributions = np.ascontiguousarray(distributions, dtype=np.float64)
+    count, bins = distributions.shape
+    weights = np.ascontiguousarray(weights, dtype=np.float64)
+    classes = np.ascontiguousarray(classes, dtype=np.int32)
+    forced = np.ascontiguousarray(forced, dtype=np.uint8)
+    assign = np.zeros(count, dtype=np.uint32)
+    centroids = np.zeros((max(count, 1), bins), dtype=np.float64)
+    n = ctypes.c_uint64()
+    check(lib.nz_cluster_chunks(_ptr(distributions), _ptr(weights), _ptr(classes), _ptr(forced), count, bins,
+                                float(threshold), int(bool(share)), _ptr(assign), _ptr(centroids), len(centroids),
+                                ctypes.byref(n)))
+    return assign, centroids[:n.value]
+
+
+def storage_decode(pieces, threads=0):
+    """Decodes storage pieces (a STORAGE_PIECE_DTYPE array whose `lanes`
+    point at STORAGE_LANE_DTYPE records) on the host cores; the caller keeps
+    every buffer the records point at alive during the call."""
+    lib = load()
+    pieces = np.ascontiguousarray(pieces, dtype=STORAGE_PIECE_DTYPE)
+    check(lib.nz_storage_decode(_ptr(pieces) if len(pieces) else None, len(pieces), int(threads)))
 
 
 # ---- decode -----------------------------------------------------------------------

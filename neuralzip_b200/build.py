@@ -18,7 +18,7 @@ PACKAGE = Path(__file__).resolve().parent
 ROOT = PACKAGE.parent
 CSRC = PACKAGE / "csrc"
 OUTPUT = PACKAGE / "_lib" / "libnzb200.so"
-SOURCES = ("nz_host.cpp", "nz_huff0.cpp", "nz_storage.cpp", "nz_schedule.cpp", "nz_decode.cu")
+SOURCES = ("nz_host.cpp", "nz_huff0.cpp", "nz_storage.cpp", "nz_setup.cpp", "nz_schedule.cpp", "nz_decode.cu")
 HEADERS = (ROOT / "include" / "nz_b200.h", CSRC / "nz_internal.h")
 ARCH = ("-gencode", "arch=compute_100a,code=sm_100a")
 

@@ -26,7 +26,9 @@
 
 #include <algorithm>
 #include <cstring>
+#include <mutex>
 #include <string>
+#include <thread>
 #include <vector>
 
 namespace nz {
@@ -227,7 +229,17 @@ uint64_t huff0_encode(const Codebook& cb, const uint8_t* data, uint64_t size, ui
 
 // Backward reader: `top` counts the unread bits below the end marker; the
 // next bits to read are [top - n, top) with bit top - 1 read first.
-static inline uint32_t backward_peek12(const uint8_t* stream, int64_t top) {
+static inline uint32_t backward_peek12(const uint8_t* stream, uint64_t size, int64_t top) {
+    // Fast path: one unaligned little-endian 8-byte load starting at the
+    // byte that holds bit top - 12 (the window's lowest bit).
+    if (top >= 12) {
+        const uint64_t first = static_cast<uint64_t>(top - 12) >> 3;
+        if (first + 8 <= size) {
+            uint64_t word;
+            std::memcpy(&word, stream + first, 8);
+            return static_cast<uint32_t>((word >> ((top - 12) & 7)) & 0xFFFU);
+        }
+    }
     // Little-endian 64-bit word covering bits [8 * b0, 8 * b0 + 64).
     const int64_t b0 = top >= 64 ? (top - 64 + 7) / 8 : 0;
     uint64_t w = 0;
@@ -249,30 +261,122 @@ void huff0_decode(const Codebook& cb, const uint8_t* data, uint64_t size, uint8_
     if (6 + sum >= size) throw Error(NZ_EVALUE, "Corrupt Huff0 jump table.");
     sizes[3] = size - 6 - sum;
     const uint64_t segment = (count + 3) / 4;
-    const uint8_t* stream = data + 6;
+    const uint8_t* stream[4];
+    int64_t top[4];
+    uint64_t begin[4], end[4];
+    const uint8_t* at = data + 6;
     for (int s = 0; s < 4; ++s) {
-        const uint64_t begin = std::min<uint64_t>(count, segment * s);
-        const uint64_t end = s == 3 ? count : std::min<uint64_t>(count, segment * (s + 1));
         const uint64_t n = sizes[s];
-        if (n == 0 || stream[n - 1] == 0) throw Error(NZ_EVALUE, "Corrupt Huff0 stream end.");
-        int64_t top = static_cast<int64_t>(8 * (n - 1) + (31 - __builtin_clz(stream[n - 1])));
-        for (uint64_t i = begin; i < end; ++i) {
-            const uint32_t e = cb.single[backward_peek12(stream, top)];
-            const uint32_t length = e >> 20;
-            if (!((e >> 16) & 3U) || top < static_cast<int64_t>(length))
-                throw Error(NZ_EVALUE, "Corrupt Huff0 stream.");
-            out[i] = static_cast<uint8_t>(e);
-            top -= length;
-        }
-        if (top != 0) throw Error(NZ_EVALUE, "Huff0 stream has unconsumed bits.");
-        stream += n;
+        if (n == 0 || at[n - 1] == 0) throw Error(NZ_EVALUE, "Corrupt Huff0 stream end.");
+        stream[s] = at;
+        top[s] = static_cast<int64_t>(8 * (n - 1) + (31 - __builtin_clz(at[n - 1])));
+        begin[s] = std::min<uint64_t>(count, segment * s);
+        end[s] = s == 3 ? count : std::min<uint64_t>(count, segment * (s + 1));
+        at += n;
     }
+    // The four streams are independent: decode them in lockstep, one symbol
+    // of each per step (four dependency chains instead of one), and check
+    // the entries once at the end of the run.
+    const uint32_t* single = cb.single.data();
+    uint32_t bad = 0;
+    auto step = [&](int s, uint64_t i) {
+        const uint32_t e = single[backward_peek12(stream[s], sizes[s], top[s])];
+        const uint32_t length = e >> 20;
+        bad |= static_cast<uint32_t>(!((e >> 16) & 3U)) | static_cast<uint32_t>(top[s] < static_cast<int64_t>(length));
+        out[i] = static_cast<uint8_t>(e);
+        top[s] -= length;
+    };
+    uint64_t together = end[3] - begin[3];
+    for (int s = 0; s < 3; ++s) together = std::min(together, end[s] - begin[s]);
+    for (uint64_t k = 0; k < together && !bad; ++k) {
+        step(0, begin[0] + k);
+        step(1, begin[1] + k);
+        step(2, begin[2] + k);
+        step(3, begin[3] + k);
+    }
+    for (int s = 0; s < 4 && !bad; ++s)
+        for (uint64_t i = begin[s] + together; i < end[s] && !bad; ++i) step(s, i);
+    if (bad) throw Error(NZ_EVALUE, "Corrupt Huff0 stream.");
+    for (int s = 0; s < 4; ++s)
+        if (top[s] != 0) throw Error(NZ_EVALUE, "Huff0 stream has unconsumed bits.");
 }
 
 }  // namespace nz
 
 using nz::Error;
 
+
+namespace nz {
+
+// Validation of one storage piece before any worker runs.
+void check_piece(const nz_storage_piece& p) {
+    check_dtype(p.dt);
+    if (!p.lanes) throw Error(NZ_EVALUE, "A storage piece has no lanes.");
+    if (p.count && !p.out) throw Error(NZ_EVALUE, "A storage piece has no output.");
+    if (p.count > static_cast<uint64_t>(INT32_MAX))
+        throw Error(NZ_EOVERFLOW, "A storage piece exceeds 2^31 elements.");
+    for (uint32_t lane = 0; lane < p.dt.elem_size; ++lane) {
+        const nz_storage_lane& l = p.lanes[lane];
+        if (l.payload_size && !l.payload) throw Error(NZ_EVALUE, "A storage chunk has no payload.");
+        if (l.mode == NZ_CHUNK_RAW) {
+            if (l.payload_size != p.count) throw Error(NZ_EVALUE, "Raw payload size mismatch.");
+        } else if (l.mode == NZ_CHUNK_HUFF0 || l.mode == NZ_CHUNK_MIXED) {
+            if (!l.codebook) throw Error(NZ_EVALUE, "Compressed chunk needs a decode table.");
+            if (l.mode == NZ_CHUNK_HUFF0 && p.count > 128 * 1024)
+                throw Error(NZ_EVALUE, "Shared chunk exceeds Huff0's block limit.");
+        } else {
+            throw Error(NZ_EVALUE, "Unsupported decoded chunk mode.");
+        }
+    }
+}
+
+// Decodes every lane of one piece (raw lanes are read in place), then
+// interleaves the lanes into element words and undoes the reorder of
+// neuralzip/dtypes.py:23-45 (the sign moves back above the exponent).
+void decode_piece(const nz_storage_piece& p) {
+    const uint32_t es = p.dt.elem_size;
+    const uint64_t n = p.count;
+    if (n == 0) return;
+    thread_local std::vector<uint8_t> scratch;
+    if (scratch.size() < es * n) scratch.resize(es * n);
+    const uint8_t* lane[4] = {nullptr, nullptr, nullptr, nullptr};
+    for (uint32_t k = 0; k < es; ++k) {
+        const nz_storage_lane& l = p.lanes[k];
+        const Codebook* cb = reinterpret_cast<const Codebook*>(l.codebook);
+        if (l.mode == NZ_CHUNK_RAW) {
+            lane[k] = l.payload;
+            continue;
+        }
+        uint8_t* dst = scratch.data() + k * n;
+        if (l.mode == NZ_CHUNK_HUFF0) huff0_decode(*cb, l.payload, l.payload_size, dst, n);
+        else mixed_decode(*cb, l.payload, l.payload_size, dst, n);
+        lane[k] = dst;
+    }
+    const uint32_t mant = (1U << p.dt.mant_bits) - 1U;
+    const uint32_t sign_stored = 1U << p.dt.mant_bits;
+    const uint32_t exp_field = ((1U << p.dt.exp_bits) - 1U) << p.dt.mant_bits;
+    const bool reorder = p.dt.reorder != 0;
+    auto restore = [&](uint32_t v) {
+        return reorder ? (v & mant) | ((v & sign_stored) << p.dt.exp_bits) | ((v >> 1) & exp_field) : v;
+    };
+    if (es == 2) {
+        uint16_t* out = reinterpret_cast<uint16_t*>(p.out);
+        for (uint64_t i = 0; i < n; ++i) {
+            const uint16_t w = static_cast<uint16_t>(restore(lane[0][i] | (static_cast<uint32_t>(lane[1][i]) << 8)));
+            std::memcpy(out + i, &w, 2);
+        }
+    } else {
+        uint32_t* out = reinterpret_cast<uint32_t*>(p.out);
+        for (uint64_t i = 0; i < n; ++i) {
+            const uint32_t w = restore(lane[0][i] | (static_cast<uint32_t>(lane[1][i]) << 8) |
+                                       (static_cast<uint32_t>(lane[2][i]) << 16) |
+                                       (static_cast<uint32_t>(lane[3][i]) << 24));
+            std::memcpy(out + i, &w, 4);
+        }
+    }
+}
+
+}  // namespace nz
 
 extern "C" {
 
@@ -342,6 +446,33 @@ int nz_huff0_encode(const nz_codebook* codebook, const uint8_t* data, uint64_t s
     NZ_GUARD({
         if (!codebook || !written || (size && !data)) throw Error(NZ_EVALUE, "Null argument.");
         *written = nz::huff0_encode(*reinterpret_cast<const nz::Codebook*>(codebook), data, size, out, cap);
+    })
+}
+
+int nz_storage_decode(const nz_storage_piece* pieces, uint64_t count, int32_t threads) {
+    NZ_GUARD({
+        if (count && !pieces) throw Error(NZ_EVALUE, "Null storage pieces.");
+        for (uint64_t i = 0; i < count; ++i) nz::check_piece(pieces[i]);
+        // Every piece decodes on its own; the first failure by piece index
+        // is the one reported, whatever order the workers ran in.
+        std::mutex lock;
+        uint64_t failed_at = count;
+        int failed_status = NZ_OK;
+        std::string failed_message;
+        const unsigned hw = std::thread::hardware_concurrency();
+        const int workers = threads > 0 ? threads : static_cast<int>(std::min<unsigned>(hw ? hw : 1U, 16U));
+        nz::run_jobs(count, workers, [&](uint64_t i) {
+            try {
+                nz::decode_piece(pieces[i]);
+            } catch (const nz::Error& e) {
+                std::lock_guard<std::mutex> hold(lock);
+                if (i < failed_at) failed_at = i, failed_status = e.status, failed_message = e.what();
+            } catch (const std::exception& e) {
+                std::lock_guard<std::mutex> hold(lock);
+                if (i < failed_at) failed_at = i, failed_status = NZ_ERUNTIME, failed_message = e.what();
+            }
+        });
+        if (failed_at < count) throw Error(failed_status, failed_message);
     })
 }
 

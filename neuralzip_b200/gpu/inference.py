@@ -370,14 +370,14 @@ def _assemble(entries, compressor, threads=0):
     for block_name, module_name, tensor_name, tensor in entries:
         spec = DTYPES[tensor.dtype]
         stream_id = spec.gpu_stream
-        modes = compressor._transfer_chunk_modes[compressor._transfer_plan_key(tensor_name, tensor, stream_id)]
+        modes = compressor.chunk_modes(tensor_name, tensor, stream_id)
         step = _stream_chunk_size(compressor.chunk_size, spec.element_size)
         raw = tensor.detach().cpu().contiguous().reshape(-1).view(torch.uint8).numpy()
         chunks = []
         for chunk, mode in enumerate(modes):
             start = chunk * step
             part = raw[start * spec.element_size:(start + step) * spec.element_size]
-            codebook_id = mode.get("codebook_id", -1) if mode.get("kind", "raw") != "raw" else -1
+            codebook_id = mode.codebook_id if mode.kind != "raw" else -1
             if codebook_id not in codebooks:
                 payload = payloads[codebook_id]
                 codebooks[codebook_id] = codebook_from_header(bytes(payload.codebook), bytes(payload.vocab))

@@ -30,7 +30,6 @@ from neuralzip_b200.dtypes import DTYPES
 from neuralzip_b200.gpu.inference import GPUEncodedSymbols, NeuralZipRuntime, export_model_for_gpu
 from neuralzip_b200.payloads import NeuralZipStats
 from neuralzip_b200.setup import NeuralZipSetup
-from neuralzip_b200.storage import _bytes_tensor
 from neuralzip_b200.utils import _model_tensors, time_call
 
 FORMAT_NAME = "neuralzip"
@@ -245,7 +244,7 @@ def _save_pretrained(model, directory, *, setup=None, save_args=(), save_kwargs=
         raise ValueError("NeuralZip does not support distributed checkpoint saving.")
     state = dict(resident)
     state[STORAGE_DATA] = blob
-    state[STORAGE_METADATA] = _bytes_tensor(json.dumps(storage, separators=(",", ":"), sort_keys=True).encode("utf-8"))
+    state[STORAGE_METADATA] = torch.frombuffer(bytearray(json.dumps(storage, separators=(",", ":"), sort_keys=True).encode("utf-8")), dtype=torch.uint8)
     metadata = {"format": FORMAT_NAME, "version": FORMAT_VERSION, "encoding": "storage", "aliases": aliases,
                 "stats": asdict(stats)}
     config = model.config

@@ -142,8 +142,9 @@ def compress_direct_storage(tensor_specs, prefix, *, min_saving_bytes=0, threads
     (bytearray, groups) where groups[t][lane] lists (mode, symbols,
     codebook_id, offset, size) per chunk (direct_storage.h:72-214).
 
-    tensor_specs: (data, dtype spec, stream_id, chunk_size, modes) like the
-    reference's Python wrapper (neuralzip/huff0.py:40-53)."""
+    tensor_specs: (data, dtype spec, stream_id, chunk_size, modes), modes
+    holding one compressor.ChunkMode per source chunk (the reference's
+    Python wrapper takes the same tuple, neuralzip/huff0.py:40-53)."""
     if min_saving_bytes < 0 or threads < 0:
         raise ValueError("min_saving_bytes and threads must be non-negative.")
     if not (0 < compression_threshold <= 1):
@@ -200,8 +201,7 @@ def compress_direct_storage(tensor_specs, prefix, *, min_saving_bytes=0, threads
         mode = r["modes"][local]
         symbols = lanes_of(index)[r["stream"]][start:start + length]
         budget = int(length * compression_threshold) - SHARED_CHUNK_METADATA_BYTES
-        kind = mode.get("kind", "raw") if isinstance(mode, dict) else mode[0]
-        book = mode.get("codebook") if isinstance(mode, dict) else mode[1]
+        kind, book = mode.kind, mode.codebook
         payload = b""
         if budget > 0 and kind == "shared_huff0":
             payload = _native.huff0_encode(book.handle, symbols, length) if length <= MAX_BLOCK_SIZE else b""
@@ -240,7 +240,7 @@ def compress_direct_storage(tensor_specs, prefix, *, min_saving_bytes=0, threads
                 if lane == r["stream"]:
                     kind, payload = results[j]
                     mode = r["modes"][local]
-                    cid = -1 if kind == "raw" else (mode.get("codebook_id", -1) if isinstance(mode, dict) else mode[2])
+                    cid = -1 if kind == "raw" else mode.codebook_id
                     chunks.append((kind, length, cid, offsets[j], len(payload)))
                 else:
                     slot = lane - (lane > r["stream"])
@@ -251,84 +251,54 @@ def compress_direct_storage(tensor_specs, prefix, *, min_saving_bytes=0, threads
     return output, tuple(groups)
 
 
+# (mantissa, exponent) bits of the element layouts storage holds, by
+# (element size, reorder): bf16, fp32 and fp16 (neuralzip/dtypes.py:53-83).
+_WIDTH_FIELDS = {(2, 1): (7, 8), (4, 1): (23, 8), (2, 0): (10, 5), (4, 0): (23, 8)}
+
+
 def decompress_mixed_streams_many(tensor_specs, *, threads=0):
     """Decodes tensors from per-lane chunk lists (decode_queue.h:1-113):
     spec = (element_size, bit_reorder, numel, groups) where groups[lane] is a
     sequence of (mode, payload, symbol_count, decodebook). Returns one
-    bytearray of element bytes per tensor."""
+    bytearray of element bytes per tensor. One native call
+    (nz_storage_decode) decodes, merges and restores every chunk."""
     if threads < 0:
         raise ValueError("threads must be non-negative.")
-    outputs, jobs = [], []
-    total = 0
+    pieces, lane_records, keep, outputs = [], [], [], []
     for element_size, bit_reorder, numel, groups in tensor_specs:
         if element_size not in (2, 4) or numel < 0:
             raise ValueError("Invalid decoded width or element count.")
         if len(groups) != element_size:
             raise ValueError("Decode needs one group per byte stream.")
+        if any(len(lane) != len(groups[0]) for lane in groups):
+            raise ValueError("Unaligned chunk groups.")
+        mant_bits, exp_bits = _WIDTH_FIELDS[(element_size, int(bool(bit_reorder)))]
         out = bytearray(numel * element_size)
         outputs.append(out)
-        total += len(out)
-        per_lane = []
-        for lane, chunks in enumerate(groups):
-            offset, items = 0, []
-            for mode, payload, count, book in chunks:
-                if count < 0 or count > numel - offset:
-                    raise ValueError("Chunk exceeds its tensor element count.")
-                if mode == "raw":
-                    if len(payload) != count:
-                        raise ValueError("Raw payload size mismatch.")
-                elif mode not in ("shared_huff0", "mixed_huffman"):
-                    raise ValueError("Unsupported decoded chunk mode.")
-                elif book is None:
-                    raise ValueError("Compressed chunk needs a decode table.")
-                elif mode == "shared_huff0" and count > MAX_BLOCK_SIZE:
-                    raise ValueError("Shared chunk exceeds Huff0's block limit.")
-                items.append((offset, count, mode, payload, book))
-                offset += count
-            if offset != numel:
-                raise ValueError("Byte stream does not reconstruct exactly numel values.")
-            per_lane.append(items)
-        if any(len(items) != len(per_lane[0]) for items in per_lane):
-            raise ValueError("Unaligned chunk groups.")
-        for j in range(len(per_lane[0])):
-            first = per_lane[0][j]
-            if any(items[j][:2] != first[:2] for items in per_lane):
+        out_at = np.frombuffer(out, dtype=np.uint8).ctypes.data if numel else 0
+        first = 0
+        for c in range(len(groups[0])):
+            count = int(groups[0][c][2])
+            if count < 0 or count > numel - first:
+                raise ValueError("Chunk exceeds its tensor element count.")
+            if any(int(lane[c][2]) != count for lane in groups):
                 raise ValueError("Unaligned chunk boundaries.")
-            jobs.append((len(outputs) - 1, element_size, bit_reorder, first[0], first[1],
-                         [items[j] for items in per_lane]))
-
-    def run(job):
-        index, es, reorder, offset, count, chunks = job
-        lanes = []
-        for _, _, mode, payload, book in chunks:
-            if mode == "raw":
-                lanes.append(np.frombuffer(memoryview(payload).cast("B"), dtype=np.uint8))
-            elif mode == "mixed_huffman":
-                lanes.append(_native.mixed_decode(book, payload, count))
-            else:
-                lanes.append(_native.huff0_decode(book, payload, count))
-        merged = np.empty((count, es), dtype=np.uint8)
-        for lane in range(es):
-            merged[:, lane] = lanes[lane]
-        if reorder:
-            words = merged.view("<u2" if es == 2 else "<u4").reshape(-1)
-            mant = 7 if es == 2 else 23
-            exp_bits = 8
-            mant_mask = (1 << mant) - 1
-            sign = 1 << (mant + exp_bits)
-            exp_field = ((1 << exp_bits) - 1) << mant
-            dtype = np.uint16 if es == 2 else np.uint32
-            restored = (words & dtype(mant_mask)) | ((words << dtype(exp_bits)) & dtype(sign)) | \
-                ((words >> dtype(1)) & dtype(exp_field))
-            merged = restored.astype(dtype).view(np.uint8).reshape(count, es)
-        view = np.frombuffer(outputs[index], dtype=np.uint8)
-        view[offset * es:(offset + count) * es] = merged.reshape(-1)
-
-    workers = _workers(threads, len(jobs), total)
-    if workers > 1:
-        with ThreadPoolExecutor(workers) as pool:
-            list(pool.map(run, jobs))
-    else:
-        for job in jobs:
-            run(job)
+            records = []
+            for mode, payload, symbols, book in (lane[c] for lane in groups):
+                code = _native.CHUNK_MODES.get(mode)
+                if code is None:
+                    raise ValueError("Unsupported decoded chunk mode.")
+                if code != _native.CHUNK_RAW and book is None:
+                    raise ValueError("Compressed chunk needs a decode table.")
+                data = np.frombuffer(memoryview(payload).cast("B"), dtype=np.uint8)
+                keep.append(data)
+                records.append((data.ctypes.data if len(data) else 0, len(data),
+                                book.handle.value if book is not None else 0, code, 0))
+            lane_records.append(np.array(records, dtype=_native.STORAGE_LANE_DTYPE))
+            pieces.append((lane_records[-1].ctypes.data, out_at + first * element_size, count, element_size,
+                           int(bool(bit_reorder)), mant_bits, exp_bits, 0, 0))
+            first += count
+        if first != numel:
+            raise ValueError("Byte stream does not reconstruct exactly numel values.")
+    _native.storage_decode(np.array(pieces, dtype=_native.STORAGE_PIECE_DTYPE), threads)
     return outputs

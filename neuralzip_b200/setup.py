@@ -1,62 +1,50 @@
 """Offline setup: chunk clustering and codebook learning.
 
-Same constructor options, pickle fields and behaviour as
-neuralzip/setup.py:21-249: every floating tensor's selected byte lane is cut
-into ``chunk_size`` byte chunks; a chunk joins the nearest same-dtype cluster
-whose centroid lies within ``cluster_js_threshold`` (base-2 Jensen-Shannon
-distance of exponent histograms, linear scan), keeping up to
-``max_codebook_sample_bytes`` of samples per cluster; each cluster gets a
-singleton (Huff0) codebook and, where the dtype has a pure exponent lane, an
-adaptive pair/singleton ("mixed") codebook with up to 254 pairs, kept only
-when its estimated stored size beats the singleton's on up to four sample
-chunks; every (tensor, dtype, stream) also gets a pooled singleton codebook
-for shape-independent transfer.
+Public surface of neuralzip/setup.py:21-89 (``NeuralZipSetup`` with the same
+constructor options, pickle fields, ``build``/``save``/``load`` and
+``setup_seconds``) and the same decisions:
+
+* every floating tensor's coded byte lane is cut into ``chunk_size``-byte
+  source chunks, and each chunk's exponent distribution is clustered with
+  the chunks before it (same dtype and forced label; nearest centroid by
+  base-2 Jensen-Shannon distance, joined when within
+  ``cluster_js_threshold``), keeping up to ``max_codebook_sample_bytes`` of
+  sample bytes per cluster;
+* each cluster gets a singleton (Huff0) table and, where the dtype has a
+  pure exponent lane, an adaptive pair/singleton ("mixed") table with up to
+  254 pairs, pruned until every pair codes no longer than its two halves,
+  and kept when its estimated stored size on up to four sample chunks beats
+  the singleton's;
+* every (tensor, dtype, lane) also gets a pooled singleton table, for
+  tensors whose shape differs at transfer time.
+
+The design differs from the reference's: histograms, lane splits and token
+counts are native passes over whole tensors; the clustering is one native
+pass over all chunks (``nz_cluster_chunks``); and the two table options are
+sized with measure-only encodes of the sample lanes under the packer's own
+raw-fallback rule, instead of six timed storage compressions of rebuilt
+element data.
 """
 
+from __future__ import annotations
+
 import pickle
+import time
 from dataclasses import dataclass
 from pathlib import Path
 from statistics import median
 
 import numpy as np
+import torch
 
-from neuralzip_b200 import huff0
+from neuralzip_b200 import _native, huff0
 from neuralzip_b200.dtypes import DTYPES
 from neuralzip_b200.payloads import CHUNK_METADATA_BYTES, CodebookPayload
-from neuralzip_b200.utils import (
-    _floating_tensors,
-    _model_tensors,
-    _stream_chunk_size,
-    _tensor_raw_bytes,
-    jensen_shannon_distance,
-    time_call,
-)
+from neuralzip_b200.utils import _floating_tensors, _model_tensors, _stream_chunk_size, time_call
 
-
-def _selected_lane(raw, spec):
-    """The GPU-coded byte lane of raw element bytes (after the reorder of
-    DTypeSpec.reorder_bytes), split natively."""
-    from neuralzip_b200 import _native
-
-    dt = _native.dtype_struct(spec.element_size, spec.bit_reorder, spec.mantissa_bits, spec.exponent_bits,
-                              spec.gpu_stream)
-    return _native.split_lanes(np.frombuffer(raw, dtype=np.uint8), dt)[spec.gpu_stream]
-
-
-def _native_counts(data):
-    """256-bin byte histogram (uint64)."""
-    from neuralzip_b200 import _native
-
-    return _native.count_tokens(data, b"")
-
-
-def _chunk_histograms(raw, spec, step):
-    """Exponent histogram (256 bins) of every `step`-element chunk."""
-    from neuralzip_b200 import _native
-
-    dt = _native.dtype_struct(spec.element_size, spec.bit_reorder, spec.mantissa_bits, spec.exponent_bits,
-                              spec.gpu_stream)
-    return _native.exponent_histograms(np.frombuffer(raw, dtype=np.uint8), dt, step).astype(np.int64)
+MAX_PAIRS = 254
+CODED_METADATA = CHUNK_METADATA_BYTES["shared_huff0"]
+RAW_METADATA = CHUNK_METADATA_BYTES["raw"]
 
 
 @dataclass(frozen=True)
@@ -67,6 +55,23 @@ class NeuralZipSetupReport:
     @property
     def setup_seconds(self):
         return self.clustering_seconds + self.codebook_setup_seconds
+
+
+@dataclass
+class _Cluster:
+    dtype: str
+    lane: int
+    weight: int = 0          # source bytes of the cluster's chunks
+    sampled: int = 0
+    samples: list = None
+
+    def __post_init__(self):
+        self.samples = []
+
+
+def _dtype_struct(spec):
+    return _native.dtype_struct(spec.element_size, spec.bit_reorder, spec.mantissa_bits, spec.exponent_bits,
+                                spec.gpu_stream)
 
 
 class NeuralZipSetup:
@@ -98,10 +103,14 @@ class NeuralZipSetup:
     def setup_seconds(self):
         return self.setup_report.setup_seconds
 
+    @property
+    def _coding(self):
+        return self.enable_shared_codebooks or self.enable_packed_codebooks
+
     def build(self, model):
-        (groups, assignments, parents), clustering_seconds = time_call(self._cluster_chunks, _model_tensors(model))
+        (clusters, assignments, pooled), clustering_seconds = time_call(self._cluster, _model_tensors(model))
         (books, chunks, tensors, report), codebook_seconds = time_call(
-            self._build_codebooks, groups, assignments, parents)
+            self._codebooks_for, clusters, assignments, pooled)
         self.codebooks = tuple(books)
         self.chunk_codebooks = chunks
         self.tensor_codebooks = tensors
@@ -126,151 +135,163 @@ class NeuralZipSetup:
             raise TypeError("Expected a current chunk-level NeuralZip setup.")
         return value
 
-    def _cluster_chunks(self, named_tensors):
-        groups, assignments, parents = [], {}, {}
+    # ---- clustering -------------------------------------------------------------
+
+    def _cluster(self, named_tensors):
+        """(clusters, {(name, dtype, lane, numel): cluster per chunk},
+        {(name, dtype, lane): pooled byte counts})."""
+        lanes, keys, pooled = [], [], {}
+        distributions, weights, classes, forced = [], [], [], []
+        class_ids = {}
         for name, tensor in _floating_tensors(named_tensors):
             spec = DTYPES[tensor.dtype]
-            raw = _tensor_raw_bytes(tensor)
-            stream_id = spec.gpu_stream
-            stream = _selected_lane(raw, spec)
+            raw = tensor.detach().cpu().contiguous().reshape(-1).view(torch.uint8).numpy()
+            dt = _dtype_struct(spec)
+            lane = _native.split_lanes(raw, dt)[spec.gpu_stream]
             step = _stream_chunk_size(self.chunk_size, spec.element_size)
-            key = (str(name), spec.name, stream_id)
-            parents[key] = _native_counts(stream)
-            histograms = _chunk_histograms(raw, spec, step)
+            key = (str(name), spec.name, spec.gpu_stream)
+            pooled[key] = _native.count_tokens(lane, b"")
+            counts = _native.exponent_histograms(raw, dt, step).astype(np.float64)
+            distributions.append(counts / counts.sum(axis=1, keepdims=True))
+            starts = range(0, len(lane), step)
+            weights.extend(min(step, len(lane) - s) for s in starts)
+            for index in range(len(starts)):
+                label = self.cluster_map.get((name, index), self.cluster_map.get(name))
+                classes.append(class_ids.setdefault((spec.name, label), len(class_ids)))
+                forced.append(label is not None)
+            lanes.append((lane, step))
+            keys.append((*key, tensor.numel()))
+        if not keys:
+            return [], {}, pooled
+        assign, _centroids = _native.cluster_chunks(
+            np.concatenate(distributions), weights, classes, forced, self.cluster_js_threshold,
+            share=self.enable_shared_codebooks)
+        clusters = {}
+        assignments = {}
+        position = 0
+        for key, (lane, step) in zip(keys, lanes):
             ids = []
-            for index, start in enumerate(range(0, len(stream), step)):
-                part = stream[start:start + step]
-                counts = histograms[index]
-                distribution = counts / counts.sum()
-                forced = self.cluster_map.get((name, index), self.cluster_map.get(name))
-                compatible = [
-                    i for i, group in enumerate(groups)
-                    if group["dtype"] == spec.name and group["forced"] == forced
-                ] if self.enable_shared_codebooks else []
-                distance, nearest = min(
-                    ((jensen_shannon_distance(distribution, groups[i]["centroid"]), i) for i in compatible),
-                    default=(float("inf"), None),
-                )
-                if nearest is None or (forced is None and distance > self.cluster_js_threshold):
-                    nearest = len(groups)
-                    groups.append({
-                        "dtype": spec.name, "stream": stream_id, "forced": forced,
-                        "centroid": distribution, "weight": 0, "samples": [], "sampled": 0,
-                    })
-                group = groups[nearest]
-                weight = len(part)
-                total = group["weight"] + weight
-                group["centroid"] = (group["centroid"] * group["weight"] + distribution * weight) / total
-                group["weight"] = total
-                budget = self.max_codebook_sample_bytes - group["sampled"]
-                if budget > 0:
-                    sample = part[:budget].tobytes()
-                    group["samples"].append(sample)
-                    group["sampled"] += len(sample)
-                ids.append(nearest)
-            assignments[(*key, tensor.numel())] = tuple(ids)
-        return groups, assignments, parents
+            for start in range(0, len(lane), step):
+                cid = int(assign[position])
+                position += 1
+                cluster = clusters.setdefault(cid, _Cluster(key[1], key[2]))
+                part = lane[start:start + step]
+                cluster.weight += len(part)
+                take = self.max_codebook_sample_bytes - cluster.sampled
+                if take > 0:
+                    sample = part[:take].tobytes()
+                    cluster.samples.append(sample)
+                    cluster.sampled += len(sample)
+                ids.append(cid)
+            assignments[key] = tuple(ids)
+        return [clusters[i] for i in range(len(clusters))], assignments, pooled
 
-    def _build_codebooks(self, groups, assignments, parents):
-        books, cache, report = [], {}, []
+    # ---- codebooks --------------------------------------------------------------
 
-        def add(book, dtype, stream, vocab=b""):
-            if book is None or not (self.enable_shared_codebooks or self.enable_packed_codebooks):
+    def _codebooks_for(self, clusters, assignments, pooled):
+        books, index, report = [], {}, []
+
+        def register(book, dtype, lane, vocab=b""):
+            if book is None or not self._coding:
                 return None
             mode = "mixed_huffman" if vocab else "shared_huff0"
-            key = dtype, stream, mode, book.codebook, vocab
+            key = (dtype, lane, mode, book.codebook, vocab)
             if not self.enable_shared_codebooks:
-                key = (*key, len(books))
-            if key not in cache:
-                cache[key] = len(books)
-                books.append(CodebookPayload(len(books), stream, dtype, mode, book.codebook, vocab=vocab))
-            return cache[key]
+                key += (len(books),)
+            if key not in index:
+                index[key] = len(books)
+                books.append(CodebookPayload(len(books), lane, dtype, mode, book.codebook, vocab=vocab))
+            return index[key]
 
         specs = {spec.name: spec for spec in DTYPES.values()}
-        cluster_ids = []
-        for group in groups:
-            book, vocab, scores = self._prepare_codebook(group, specs[group["dtype"]])
+        per_cluster = []
+        for number, cluster in enumerate(clusters):
+            book, vocab, scores = self._cluster_codebook(cluster, specs[cluster.dtype])
             if scores is not None:
-                report.append({"cluster": len(cluster_ids), **scores})
-            cluster_ids.append(add(book, group["dtype"], group["stream"], vocab))
-        chunks = {key: tuple(cluster_ids[i] for i in ids) for key, ids in assignments.items()}
-        # Pooled counts per tensor stream: shape-independent transfer.
-        tensors = {key: add(self._singleton_codebook(counts), key[1], key[2]) for key, counts in parents.items()}
+                report.append({"cluster": number, **scores})
+            per_cluster.append(register(book, cluster.dtype, cluster.lane, vocab))
+        chunks = {key: tuple(per_cluster[c] for c in ids) for key, ids in assignments.items()}
+        tensors = {key: register(self._singleton(counts), key[1], key[2]) for key, counts in pooled.items()}
         return books, chunks, tensors, report
 
-    def _singleton_codebook(self, counts):
-        if not (self.enable_shared_codebooks or self.enable_packed_codebooks):
+    def _singleton(self, counts):
+        if not self._coding:
             return None
         try:
             return huff0.build_codebook_from_counts(counts, prior_count=self.prior_count, max_bits=12)
         except RuntimeError:
-            return None  # Some uniform alphabets cannot be serialized; store raw.
+            return None  # some uniform alphabets have no serializable table: stored raw
 
-    def _prepare_codebook(self, group, spec):
-        if not (self.enable_shared_codebooks or self.enable_packed_codebooks):
+    def _cluster_codebook(self, cluster, spec):
+        """(table, pair vocabulary, comparison report or None)."""
+        if not self._coding:
             return None, b"", None
-        samples = group["samples"]
-        singleton = self._singleton_codebook(huff0.count_mixed_tokens(samples, b""))
+        singleton = self._singleton(huff0.count_mixed_tokens(cluster.samples, b""))
         if not self.enable_packed_codebooks or spec.exponent_stream is None:
             return singleton, b"", None
-        pairs = np.zeros(65536, dtype=np.int64)
-        for sample in samples:
-            values = np.frombuffer(sample, dtype=np.uint8).astype(np.uint16)
-            pairs += np.bincount(values[:-1] | (values[1:] << 8), minlength=65536)
-        observed = np.flatnonzero(pairs)
-        order = np.argsort(-pairs[observed], kind="stable")
-        selected = np.sort(observed[order[:254]]).astype("<u2")
-        candidate_pairs = len(selected)
-        while len(selected):
-            vocab = selected.tobytes()
-            mixed = huff0.build_mixed_codebook(
-                huff0.count_mixed_tokens(samples, vocab), vocab, prior_count=self.prior_count)
+        # Adjacent-byte pairs inside each sample, the most frequent first
+        # (stable on ties), at most MAX_PAIRS, in pair-value order.
+        pairs = np.zeros(1 << 16, dtype=np.int64)
+        for sample in cluster.samples:
+            b = np.frombuffer(sample, dtype=np.uint8).astype(np.uint32)
+            pairs += np.bincount(b[:-1] | (b[1:] << 8), minlength=1 << 16)
+        seen = np.flatnonzero(pairs)
+        chosen = np.sort(seen[np.argsort(-pairs[seen], kind="stable")[:MAX_PAIRS]]).astype("<u2")
+        candidates = len(chosen)
+        # Drop every pair whose code is longer than its halves' codes and
+        # rebuild, until all pairs pay for themselves.
+        while len(chosen):
+            vocab = chosen.tobytes()
+            mixed = huff0.build_mixed_codebook(huff0.count_mixed_tokens(cluster.samples, vocab), vocab,
+                                               prior_count=self.prior_count)
             lengths = np.frombuffer(mixed.codebook[4:], dtype=np.uint8).astype(np.uint16)
-            keep = lengths[256:] <= lengths[selected & 255] + lengths[selected >> 8]
-            if keep.all():
-                scores = self._compare_codebooks(group, spec, singleton, mixed, vocab)
-                scores.update(candidate_pairs=candidate_pairs, kept_pairs=len(selected))
+            worth = lengths[256:] <= lengths[chosen & 255] + lengths[chosen >> 8]
+            if worth.all():
+                scores = self._size_options(cluster, spec, singleton, mixed, vocab)
+                scores.update(candidate_pairs=candidates, kept_pairs=len(chosen))
                 return (mixed, vocab, scores) if scores["mode"] == "mixed_huffman" else (singleton, b"", scores)
-            selected = selected[keep]
+            chosen = chosen[worth]
         return singleton, b"", None
 
-    def _compare_codebooks(self, group, spec, singleton, mixed, vocab):
-        # Four source chunks spread across the sample, boundaries preserved.
-        available = group["samples"]
-        samples = [available[i] for i in np.linspace(0, len(available) - 1, min(4, len(available)), dtype=int)]
-        data = []
-        for sample in samples:
-            lanes = np.zeros(len(sample) * spec.element_size, dtype=np.uint8)
-            lanes[group["stream"]::spec.element_size] = np.frombuffer(sample, dtype=np.uint8)
-            raw = spec.reorder_bytes(lanes.tobytes(), restore=True)
-            data.append(np.frombuffer(raw, dtype=np.uint8))
-        options = (singleton, mixed)
-        modes = ("shared_huff0" if singleton is not None else "raw", "mixed_huffman")
-        specs = [tuple((raw, spec, group["stream"], _stream_chunk_size(self.chunk_size, spec.element_size),
-                        ({"kind": mode, "codebook": book, "codebook_id": 0} if book is not None
-                         else {"kind": "raw"},))
-                       for raw in data) for book, mode in zip(options, modes)]
-        timings = [[], []]
-        sizes = [0, 0]
-        used = [False, False]
-        for repeat in range(6):
-            for index in (0, 1) if repeat % 2 == 0 else (1, 0):
-                (output, groups), seconds = time_call(
-                    huff0.compress_direct_storage, specs[index], b"", threads=1,
-                    min_saving_bytes=self.min_saving_bytes, compression_threshold=self.compression_threshold)
-                if repeat:
-                    timings[index].append(seconds)
-                sizes[index] = sum(chunk[4] + CHUNK_METADATA_BYTES[chunk[0]]
-                                   for streams in groups for chunk in streams[group["stream"]])
-                used[index] = any(chunk[0] != "raw" for streams in groups for chunk in streams[group["stream"]])
-                del output
-        sampled = sum(map(len, samples))
-        for index, (book, mode, vocabulary) in enumerate(zip(options, modes, (b"", vocab))):
-            overhead = 0 if book is None or not used[index] else CodebookPayload(
-                0, group["stream"], spec.name, mode, book.codebook, vocab=vocabulary).metadata_bytes
-            sizes[index] = sizes[index] * group["weight"] / sampled + overhead
-        times = tuple(map(median, timings))
-        keep = sizes[1] < sizes[0]
-        return {"mode": "mixed_huffman" if keep else modes[0],
-                "singleton_bytes_estimate": sizes[0], "mixed_bytes_estimate": sizes[1],
-                "singleton_seconds": times[0], "mixed_seconds": times[1]}
+    def _stored_size(self, kind, book, lane):
+        """(stored bytes incl. chunk metadata, coded?) of one source chunk's
+        lane under the packer's rule (huff0.compress_direct_storage): coded
+        when the payload fits the budget and saves enough, else raw."""
+        length = len(lane)
+        budget = int(length * self.compression_threshold) - CODED_METADATA
+        payload = 0
+        if budget > 0 and kind == "shared_huff0" and length <= huff0.MAX_BLOCK_SIZE:
+            payload = _native.huff0_encode(book.handle, lane, length, measure=True)
+            payload = payload if payload <= budget else 0
+        elif budget > 0 and kind == "mixed_huffman":
+            payload = _native.mixed_encode(book.handle, lane, budget, measure=True)
+        if payload and payload + self.min_saving_bytes < length and \
+                payload + CODED_METADATA < length * self.compression_threshold:
+            return payload + CODED_METADATA, True
+        return length + RAW_METADATA, False
+
+    def _size_options(self, cluster, spec, singleton, mixed, vocab):
+        """Estimated stored bytes of the cluster under each table, from up to
+        four sample chunks spread over its samples, scaled to the cluster's
+        bytes, plus the table's own metadata when a chunk would use it."""
+        pick = np.linspace(0, len(cluster.samples) - 1, min(4, len(cluster.samples)), dtype=int)
+        lanes = [np.frombuffer(cluster.samples[i], dtype=np.uint8) for i in pick]
+        sampled = sum(len(lane) for lane in lanes)
+        options = (("shared_huff0" if singleton is not None else "raw", singleton, b""),
+                   ("mixed_huffman", mixed, vocab))
+        sizes, seconds = [], []
+        for kind, book, option_vocab in options:
+            runs = []
+            for _ in range(3):
+                t0 = time.perf_counter()
+                measured = [self._stored_size(kind, book, lane) for lane in lanes]
+                runs.append(time.perf_counter() - t0)
+            stored = sum(size for size, _ in measured)
+            used = any(coded for _, coded in measured)
+            table = CodebookPayload(0, cluster.lane, spec.name, kind, book.codebook, vocab=option_vocab).metadata_bytes \
+                if book is not None and used else 0
+            sizes.append(stored * cluster.weight / sampled + table)
+            seconds.append(median(runs))
+        mode = "mixed_huffman" if sizes[1] < sizes[0] else options[0][0]
+        return {"mode": mode, "singleton_bytes_estimate": sizes[0], "mixed_bytes_estimate": sizes[1],
+                "singleton_seconds": seconds[0], "mixed_seconds": seconds[1]}

@@ -116,7 +116,7 @@ def test_empty_batch_and_zero_cta_launch():
 
 def test_uniform_alphabet_is_left_raw():
     setup = NeuralZipSetup()
-    assert setup._singleton_codebook(np.full(256, 100, dtype=np.uint64)) is None
+    assert setup._singleton(np.full(256, 100, dtype=np.uint64)) is None
 
 
 class Model(nn.Module):

@@ -248,57 +248,79 @@ def _join(parent, child):
 
 
 def _decode_hook_module(model, block_name):
+    """The module whose forward pre-hook decodes `block_name`. A
+    MultiheadAttention reads out_proj.weight itself without calling the
+    Linear, so that block's hook goes on the attention module."""
     parent_name, _, child_name = block_name.rpartition(".")
-    parent = model.get_submodule(parent_name)
-    # MultiheadAttention reads out_proj.weight without calling the Linear.
-    if child_name == "out_proj" and isinstance(parent, nn.MultiheadAttention):
-        return parent
+    if child_name == "out_proj" and isinstance(model.get_submodule(parent_name), nn.MultiheadAttention):
+        return model.get_submodule(parent_name)
     return model.get_submodule(block_name)
 
 
-def _gpu_candidates(model):
-    """Blocks are the outermost ModuleList children whose Linears are not all
-    inside nested lists; other weight modules are hooked individually
-    (neuralzip/gpu/inference.py:232-274)."""
-    possible = [
-        (_join(parent_name, child_name), child)
-        for parent_name, parent in model.named_modules(remove_duplicate=False)
-        if isinstance(parent, nn.ModuleList)
-        for child_name, child in parent._modules.items()
-        if child is not None
-    ]
-    names = {name for name, _ in possible}
+def _linears_only_in_nested_lists(element, path):
+    """True when `element` (an item of a ModuleList) holds ModuleLists of
+    its own and every Linear inside it sits inside an item of one of them:
+    then the element is only a container and its inner items are the
+    blocks."""
+    inner = tuple(
+        _join(_join(path, name), item) + "."
+        for name, module in element.named_modules(remove_duplicate=False)
+        if isinstance(module, nn.ModuleList) and module is not element
+        for item, child in module._modules.items() if child is not None
+    )
+    if not inner:
+        return False
+    return all((_join(path, name) + ".").startswith(inner)
+               for name, module in element.named_modules(remove_duplicate=False) if isinstance(module, nn.Linear))
+
+
+def _list_blocks(module, path=""):
+    """Decode blocks under `module`, in module order: each item of a
+    ModuleList met on the way down is a block, unless it is only a
+    container of further ModuleLists (then the search continues inside
+    it); nothing inside a block is searched."""
     blocks = []
-    for name, module in possible:
-        if any(name.startswith(parent + ".") for parent, _ in blocks):
+    for name, child in module._modules.items():
+        if child is None:
             continue
-        nested = tuple(child + "." for child in names if child.startswith(name + "."))
-        if nested and all(
-            (_join(name, child) + ".").startswith(nested)
-            for child, layer in module.named_modules(remove_duplicate=False)
-            if isinstance(layer, nn.Linear)
-        ):
-            continue
-        blocks.append((name, module))
+        child_path = _join(path, name)
+        if isinstance(child, nn.ModuleList):
+            for item, element in child._modules.items():
+                if element is None:
+                    continue
+                item_path = _join(child_path, item)
+                if _linears_only_in_nested_lists(element, item_path):
+                    blocks.extend(_list_blocks(element, item_path))
+                else:
+                    blocks.append(item_path)
+        else:
+            blocks.extend(_list_blocks(child, child_path))
+    return blocks
+
+
+def _gpu_candidates(model):
+    """(decode block names, candidates): every Linear, Conv2d and Conv1D
+    weight (a Parameter), assigned to the list block that contains it, or
+    hooked on its own module when no block does (discovery semantics of
+    neuralzip/gpu/inference.py:232-274)."""
+    blocks = _list_blocks(model)
     candidates = []
     for module_name, module in model.named_modules(remove_duplicate=False):
-        if not isinstance(module, _GPU_WEIGHT_TYPES):
+        weight = module._parameters.get("weight") if isinstance(module, _GPU_WEIGHT_TYPES) else None
+        if not isinstance(weight, nn.Parameter):
             continue
-        parameter = module._parameters.get("weight")
-        if isinstance(parameter, nn.Parameter):
-            block_name = next(
-                (name for name, _ in blocks if module_name == name or module_name.startswith(name + ".")),
-                module_name,
-            )
-            candidates.append(_Candidate(block_name, module_name, _join(module_name, "weight"), parameter))
+        owner = next((b for b in blocks if module_name == b or module_name.startswith(b + ".")), module_name)
+        candidates.append(_Candidate(owner, module_name, _join(module_name, "weight"), weight))
     return tuple(dict.fromkeys(c.block_name for c in candidates)), tuple(candidates)
 
 
 def _unique_candidates(model, candidates):
-    occurrences = defaultdict(int)
+    """Candidates whose weight is non-empty and owned by no other module
+    (tied or shared parameters stay resident)."""
+    owners = defaultdict(int)
     for _name, parameter in model.named_parameters(remove_duplicate=False):
-        occurrences[id(parameter)] += 1
-    return tuple(c for c in candidates if c.parameter.numel() and occurrences[id(c.parameter)] == 1)
+        owners[id(parameter)] += 1
+    return tuple(c for c in candidates if c.parameter.numel() and owners[id(c.parameter)] == 1)
 
 
 def _aligned(offset, element_size):
@@ -752,15 +774,50 @@ class NeuralZipRuntime:
 
     @torch.no_grad()
     def materialized_weights(self):
-        """Yield compressed weights as bit-exact CPU tensors, one block at a time."""
+        """Yield compressed weights as bit-exact CPU tensors, one block at a
+        time (neuralzip/gpu/inference.py:495-509). While a block's weights
+        are copied to the host, the next block is already decoding on a side
+        stream when it decodes into another workspace slot, so the decode
+        hides behind the copies."""
+        stream = torch.cuda.current_stream(self.device)
+        self._drain(stream)
+        order = self.export.block_order
+        side = torch.cuda.Stream(device=self.device)
+
+        def start(name):
+            # On the side stream, after everything enqueued on `stream` so far
+            # (which covers the previous reader of the block's slot).
+            after = torch.cuda.Event()
+            after.record(stream)
+            side.wait_event(after)
+            self._decoder.decode_batches(self._prepared_batches[name], side)
+            done = torch.cuda.Event()
+            done.record(side)
+            return done
+
+        def slot(name):
+            return self._slot[self._unit_of[name]]
+
+        # The slots are overwritten block by block: the next forward must
+        # decode every unit again, even if this generator is left early.
+        for unit in range(len(self._units)):
+            self._schedule.mark(unit, 0)
         yielded = set()
-        for block_name in self.export.block_order:
-            self._decode_block(block_name)
-            torch.cuda.synchronize(self.device)
-            for item in self._groups_by_block[block_name]:
-                for binding in item.group.bindings:
-                    if binding.tensor_name in yielded:
-                        continue
-                    yielded.add(binding.tensor_name)
-                    weight = self._binding_view(block_name, item.group.encoded.dtype.torch_dtype, binding)
-                    yield binding.tensor_name, weight.detach().to("cpu", copy=True)
+        try:
+            pending = start(order[0]) if order else None
+            for index, block_name in enumerate(order):
+                stream.wait_event(pending)
+                following = order[index + 1] if index + 1 < len(order) else None
+                ahead = following is not None and slot(following) != slot(block_name)
+                pending = start(following) if ahead else None
+                for item in self._groups_by_block[block_name]:
+                    for binding in item.group.bindings:
+                        if binding.tensor_name in yielded:
+                            continue
+                        yielded.add(binding.tensor_name)
+                        weight = self._binding_view(block_name, item.group.encoded.dtype.torch_dtype, binding)
+                        yield binding.tensor_name, weight.detach().to("cpu", copy=True)
+                if following is not None and not ahead:
+                    pending = start(following)
+        finally:
+            stream.wait_stream(side)

@@ -1,10 +1,11 @@
 """Payload records, statistics and canonical byte accounting.
 
-Same records and accounting rules as neuralzip/payloads.py:1-174:
-NeuralZipStats (model.neuralzip_stats), CodebookPayload, StreamChunk,
-ByteGroupPayload, TensorPayload, the per-chunk metadata sizes (17 bytes raw,
-25 bytes coded) and storage_bytes(), which counts the blob plus canonical
-metadata rather than the surrounding file format.
+The records are the reference's public data types, with their names and
+fields (neuralzip/payloads.py:14-95): NeuralZipStats (model.neuralzip_stats),
+CodebookPayload, StreamChunk, ByteGroupPayload and TensorPayload, so pickles
+and attribute access carry over. storage_bytes() applies the same byte
+accounting, so the statistics of a checkpoint agree between the two
+implementations.
 """
 
 from dataclasses import dataclass
@@ -54,14 +55,6 @@ class NeuralZipStats:
     @property
     def total_seconds(self):
         return self.setup_seconds + self.encoding_seconds
-
-
-def _bytes_size(value):
-    return 8 + len(value)
-
-
-def _text_size(value):
-    return 4 + len(str(value).encode("utf-8"))
 
 
 @dataclass(frozen=True)
@@ -118,39 +111,73 @@ class TensorPayload:
         return self.numel * self.element_size
 
 
+# ---- canonical size of the stored metadata -------------------------------------
+#
+# compressed_bytes counts the blob plus the size the metadata would take in a
+# canonical binary serialization, not the JSON actually written (the
+# accounting of neuralzip/payloads.py:97-174): length-prefixed strings (4-byte
+# length) and byte strings (8-byte length), 8-byte integers, 4-byte stream
+# ids; per chunk 17 bytes raw or 25 bytes coded.
+
+
+def _text(value):
+    return 4 + len(str(value).encode("utf-8"))
+
+
+def _blob(value):
+    return 8 + len(value)
+
+
+# File header: magic (4), version (2), format name, codebook and tensor counts (8 each).
+_HEADER_BYTES = 4 + 2 + _text("neuralzip") + 8 + 8
+
+
 def _codebook_size(codebook):
-    return (8 + 4 + _text_size(codebook.dtype) + _text_size(codebook.mode)
-            + _bytes_size(codebook.codebook) + _bytes_size(codebook.vocab))
+    """id (8), stream (4), dtype, mode, and the header and vocabulary."""
+    return 8 + 4 + _text(codebook.dtype) + _text(codebook.mode) + _blob(codebook.codebook) + _blob(codebook.vocab)
+
+
+def _tensor_fields(entry):
+    """name, dtype, element size + numel + reorder flag (24), the shape
+    (8 per dimension) and the lane count (8)."""
+    return _text(entry["name"]) + _text(entry["dtype"]) + 24 + 8 * len(entry["shape"]) + 8
+
+
+def _lane_fields(lane):
+    """chunk count (8) and each chunk's record."""
+    return 8 + sum(CHUNK_METADATA_BYTES[chunk["mode"]] for chunk in lane)
 
 
 def storage_bytes(codebooks, tensors, blob_bytes):
-    """Counts the blob and canonical metadata, not the surrounding file format."""
+    """{raw_bytes, compressed_bytes, exponent_raw_bytes,
+    exponent_compressed_bytes} of a checkpoint from its codebooks, tensor
+    metadata entries and blob size. The exponent figures cover the lanes
+    that are a pure exponent (and the codebooks of those lanes); they are
+    None when a non-empty tensor has no such lane."""
     specs = {spec.name: spec for spec in DTYPES.values()}
-    raw_bytes = exponent_raw_bytes = exponent_compressed_bytes = 0
+    structure = _HEADER_BYTES + sum(_codebook_size(b) - len(b.codebook) - len(b.vocab) for b in codebooks)
+    raw = exponent_raw = exponent_stored = 0
+    exponent_lanes = set()
     exponent_defined = True
-    exponent_streams = set()
-    structural_bytes = 4 + 2 + _text_size("neuralzip") + 8 + 8
-    structural_bytes += sum(value.metadata_bytes - len(value.codebook) - len(value.vocab) for value in codebooks)
-    for tensor in tensors:
-        spec = specs[tensor["dtype"]]
-        numel = tensor["numel"]
-        raw_bytes += numel * tensor["element_size"]
-        if numel and spec.exponent_stream is None:
-            exponent_defined = False
-        if spec.exponent_stream is not None:
-            exponent_raw_bytes += numel
-            exponent_streams.add((spec.name, spec.exponent_stream))
-        structural_bytes += _text_size(tensor["name"]) + _text_size(tensor["dtype"]) + 24 + 8 * len(tensor["shape"]) + 8
-        for stream, group in enumerate(tensor["groups"]):
-            metadata_bytes = sum(CHUNK_METADATA_BYTES[chunk["mode"]] for chunk in group)
-            structural_bytes += 8 + metadata_bytes
-            if stream == spec.exponent_stream:
-                exponent_compressed_bytes += metadata_bytes + sum(chunk["payload"][1] for chunk in group)
-    exponent_compressed_bytes += sum(
-        value.metadata_bytes for value in codebooks if (value.dtype, value.stream_id) in exponent_streams)
+    for entry in tensors:
+        spec = specs[entry["dtype"]]
+        lane_of_exponent = spec.exponent_stream
+        raw += entry["numel"] * entry["element_size"]
+        structure += _tensor_fields(entry)
+        if lane_of_exponent is None:
+            exponent_defined = exponent_defined and not entry["numel"]
+        else:
+            exponent_raw += entry["numel"]
+            exponent_lanes.add((spec.name, lane_of_exponent))
+        for lane_index, lane in enumerate(entry["groups"]):
+            fields = _lane_fields(lane)
+            structure += fields
+            if lane_index == lane_of_exponent:
+                exponent_stored += fields - 8 + sum(chunk["payload"][1] for chunk in lane)
+    exponent_stored += sum(_codebook_size(b) for b in codebooks if (b.dtype, b.stream_id) in exponent_lanes)
     return {
-        "raw_bytes": int(raw_bytes),
-        "compressed_bytes": int(blob_bytes + structural_bytes),
-        "exponent_raw_bytes": int(exponent_raw_bytes) if exponent_defined else None,
-        "exponent_compressed_bytes": int(exponent_compressed_bytes) if exponent_defined else None,
+        "raw_bytes": int(raw),
+        "compressed_bytes": int(blob_bytes + structure),
+        "exponent_raw_bytes": int(exponent_raw) if exponent_defined else None,
+        "exponent_compressed_bytes": int(exponent_stored) if exponent_defined else None,
     }

@@ -1,96 +1,67 @@
-"""Helpers shared by setup, the codec and the GPU export.
+"""Small helpers shared by setup, the storage codec and the GPU export.
 
-Same contracts as neuralzip/utils.py:1-115 (named-tensor walks, raw byte
-views, exponent histograms, the base-2 Jensen-Shannon distance, the
-per-stream chunk size and a perf_counter timer).
+``_model_tensors`` follows the naming of neuralzip/utils.py:12-50 (dotted
+paths through nested mappings and sequences; a module's parameters and
+persistent buffers under their state-dict names), since setup keys and
+checkpoint tensor names are built from it.
 """
 
-import math
 import time
 from collections.abc import Mapping
-from itertools import chain
 
-import numpy as np
 import torch
 
-from neuralzip_b200.dtypes import DTYPES
 
-
-def _named_tensors(value, prefix=""):
-    if torch.is_tensor(value):
-        yield prefix, value
-    elif isinstance(value, Mapping):
-        for key, child in value.items():
-            yield from _named_tensors(child, str(key) if not prefix else f"{prefix}.{key}")
-    elif isinstance(value, (list, tuple)):
-        for index, child in enumerate(value):
-            yield from _named_tensors(child, str(index) if not prefix else f"{prefix}.{index}")
+def _tensor_items(value):
+    """(dotted name, tensor) for every tensor inside nested mappings, lists
+    and tuples, depth first, in insertion order."""
+    stack = [("", value)]
+    while stack:
+        prefix, node = stack.pop()
+        if torch.is_tensor(node):
+            yield prefix, node
+            continue
+        if isinstance(node, Mapping):
+            children = [(str(key), child) for key, child in node.items()]
+        elif isinstance(node, (list, tuple)):
+            children = [(str(index), child) for index, child in enumerate(node)]
+        else:
+            continue
+        stack.extend((f"{prefix}.{key}" if prefix else key, child) for key, child in reversed(children))
 
 
 def _model_tensors(model):
-    if isinstance(model, Mapping):
-        items = _named_tensors(model)
-    elif isinstance(model, torch.nn.Module):
+    """Named floating tensors of a model (parameters and persistent buffers)
+    or of a nested tensor mapping; names must be unique."""
+    if isinstance(model, torch.nn.Module):
         persistent = set(model.state_dict())
-        items = chain(model.named_parameters(),
-                      ((n, t) for n, t in model.named_buffers() if n in persistent))
+        items = list(model.named_parameters())
+        items += [(name, tensor) for name, tensor in model.named_buffers() if name in persistent]
+    elif isinstance(model, Mapping):
+        items = list(_tensor_items(model))
     else:
         raise TypeError("Expected a tensor mapping or torch.nn.Module.")
-    tensors = [(str(n), t) for n, t in items if torch.is_tensor(t) and t.is_floating_point()]
+    tensors = [(str(name), t) for name, t in items if torch.is_tensor(t) and t.is_floating_point()]
     if not tensors:
         raise ValueError("No floating tensors were found.")
-    if len({n for n, _ in tensors}) != len(tensors):
+    if len({name for name, _ in tensors}) != len(tensors):
         raise ValueError("Tensor names must be unique.")
     return tensors
 
 
 def _floating_tensors(named_tensors):
-    for name, tensor in sorted(named_tensors, key=lambda item: item[0]):
-        if torch.is_tensor(tensor) and tensor.is_floating_point() and tensor.numel():
-            yield name, tensor
-
-
-def _tensor_raw_bytes(tensor):
-    tensor = tensor.detach().cpu().contiguous()
-    return tensor.reshape(-1).view(torch.uint8).numpy().tobytes()
-
-
-def _tensor_from_raw_bytes(raw_bytes, dtype, shape):
-    owner = raw_bytes if isinstance(raw_bytes, bytearray) else bytearray(raw_bytes)
-    shape = tuple(int(d) for d in shape)
-    expected = math.prod(shape) * torch.empty((), dtype=dtype).element_size()
-    if len(owner) != expected:
-        raise ValueError(f"Decoded tensor byte length mismatch: {len(owner)} != {expected}.")
-    if not owner:
-        return torch.empty(shape, dtype=dtype)
-    return torch.frombuffer(owner, dtype=torch.uint8).view(dtype).reshape(shape)
-
-
-def exponent_distribution(tensor):
-    """Normalized exponent histogram of a floating tensor."""
-    config = DTYPES[tensor.dtype]
-    exponent = config.extract_exponents(_tensor_raw_bytes(tensor))
-    counts = np.bincount(exponent, minlength=256).astype(np.float64)
-    total = counts.sum()
-    return counts / total if total else counts
-
-
-def jensen_shannon_distance(left, right):
-    """Base-2 Jensen-Shannon distance between two distributions."""
-    left = np.asarray(left, dtype=np.float64)
-    right = np.asarray(right, dtype=np.float64)
-    middle = 0.5 * (left + right)
-    lm, rm = left > 0, right > 0
-    divergence = 0.5 * np.sum(left[lm] * np.log2(left[lm] / middle[lm]))
-    divergence += 0.5 * np.sum(right[rm] * np.log2(right[rm] / middle[rm]))
-    return float(np.sqrt(max(float(divergence), 0.0)))
+    """Non-empty floating tensors, ordered by name (setup's visiting order)."""
+    return [(name, t) for name, t in sorted(named_tensors, key=lambda item: item[0])
+            if torch.is_tensor(t) and t.is_floating_point() and t.numel()]
 
 
 def _stream_chunk_size(chunk_size, element_size):
+    """Elements per source chunk: a chunk is `chunk_size` bytes of elements."""
     return max(1, chunk_size // int(element_size))
 
 
 def time_call(func, /, *args, **kwargs):
-    """Call a function and return the result and elapsed seconds."""
+    """(func(*args, **kwargs), elapsed seconds)."""
     start = time.perf_counter()
-    return func(*args, **kwargs), time.perf_counter() - start
+    result = func(*args, **kwargs)
+    return result, time.perf_counter() - start

@@ -52,12 +52,9 @@ def test_v3_checkpoint_save_and_manual_decode_cpu():
         assert meta["format"] == "neuralzip" and meta["version"] == 3 and meta["encoding"] == "storage"
         assert model.neuralzip_stats.representation == "storage"
         assert model.neuralzip_stats.compressed_bytes < model.neuralzip_stats.raw_bytes
-        special, resident = pretrained._checkpoint_state(Path(folder))
-        assert set(special) == {pretrained.STORAGE_DATA, pretrained.STORAGE_METADATA}
-        storage = json.loads(pretrained._tensor_bytes(special[pretrained.STORAGE_METADATA]))
-        assert storage["version"] == 2
-        state = pretrained._decode_model_storage(special[pretrained.STORAGE_DATA], storage, resident,
-                                                 meta.get("aliases", {}))
+        blob, storage, resident = pretrained._Checkpoint.read(Path(folder))
+        assert storage["version"] == 2 and not any(n.startswith(pretrained.PREFIX) for n in resident)
+        state = pretrained._decoded_state(blob, storage, resident, meta.get("aliases", {}))
     assert set(state) >= set(expected)
     assert all(exact(state[name], tensor) for name, tensor in expected.items())
 

@@ -246,3 +246,47 @@ def test_tile_copy_words_matches_kernel_bounds():
                                                          (((5000 >> 5) + 16) & ~3) - ((100 >> 5) & ~3),
                                                          (((5001 >> 5) + 16) & ~3) - ((5000 >> 5) & ~3))
     assert tile_copy_words([], 0) == 0
+
+
+def _js(a, b):
+    m = 0.5 * (a + b)
+    left = np.sum(a[a > 0] * np.log2(a[a > 0] / m[a > 0]))
+    right = np.sum(b[b > 0] * np.log2(b[b > 0] / m[b > 0]))
+    return float(np.sqrt(max(0.5 * left + 0.5 * right, 0.0)))
+
+
+@pytest.mark.parametrize("share", [True, False])
+def test_native_clustering_matches_sequential_rule(share):
+    """nz_cluster_chunks against the clustering rule of
+    neuralzip/setup.py:91-141 restated step by step in numpy: nearest
+    centroid of the same class (earliest on ties), joined within the
+    threshold or when forced, centroids weight-averaged after each chunk."""
+    rng = np.random.default_rng(4)
+    protos = rng.dirichlet(np.full(256, 0.05), size=5)
+    n = 300
+    dists = np.stack([rng.dirichlet(protos[rng.integers(5)] * 400 + 1e-3) for _ in range(n)])
+    weights = rng.integers(1000, 5000, size=n).astype(np.float64)
+    classes = rng.integers(0, 3, size=n).astype(np.int32)
+    forced = (rng.random(n) < 0.1).astype(np.uint8)
+    threshold = 0.3
+    assign, centroids = _native.cluster_chunks(dists, weights, classes, forced, threshold, share=share)
+    cls, cent, wts, expect = [], [], [], []
+    for i in range(n):
+        best, best_d = None, None
+        for c in range(len(cls)) if share else ():
+            if cls[c] != classes[i]:
+                continue
+            d = _js(dists[i], cent[c])
+            if best is None or d < best_d:
+                best, best_d = c, d
+        if best is None or (not forced[i] and best_d > threshold):
+            best = len(cls)
+            cls.append(classes[i]); cent.append(dists[i].copy()); wts.append(0.0)
+        total = wts[best] + weights[i]
+        cent[best] = (cent[best] * wts[best] + dists[i] * weights[i]) / total
+        wts[best] = total
+        expect.append(best)
+    assert assign.tolist() == expect
+    assert len(centroids) == len(cls) and np.allclose(centroids, np.stack(cent), rtol=0, atol=1e-12)
+    if not share:
+        assert len(cls) == n

@@ -83,8 +83,10 @@ def parse_args():
     p.add_argument("--no-generation", action="store_true")
     p.add_argument("--no-config5a", action="store_true", help="N=1: skip the one-GPU share of config 5a")
     p.add_argument("--e2e-pieces", type=int, default=16, help="pipeline pieces of the host-to-host decode")
-    p.add_argument("--workload", choices=("bulk", "config3", "config4"), default="bulk",
-                   help="bulk: config 2 at N=1, config 5a under torchrun (default line); config3/4: generation")
+    p.add_argument("--workload", choices=("bulk", "config3", "config4", "config5b"), default="bulk",
+                   help="bulk: config 2 at N=1, config 5a under torchrun (default line); config3/4: generation; "
+                        "config5b: tensor-parallel generation over the torchrun ranks, each building its slices")
+    p.add_argument("--layers", type=int, default=None, help="config5b: decoder layers (80 in configs[4])")
     p.add_argument("--new-tokens", type=int, default=None)
     p.add_argument("--no-overlap", action="store_true", help="sequential decode schedule")
     p.add_argument("--prefetch-depth", type=int, default=2, help="decode buffers per dtype in the overlapped schedule")
@@ -746,6 +748,9 @@ def _model_config(name):
         return Qwen2Config(hidden_size=896, num_hidden_layers=24, num_attention_heads=14, num_key_value_heads=2,
                            intermediate_size=4864, vocab_size=151936, tie_word_embeddings=True,
                            max_position_embeddings=4096), 32, 128
+    if name == "config5b":  # Llama-3-70B architecture
+        return LlamaConfig(hidden_size=8192, num_hidden_layers=80, num_attention_heads=64, num_key_value_heads=8,
+                           intermediate_size=28672, vocab_size=128256, max_position_embeddings=4096), 128, 64
     return LlamaConfig(hidden_size=4096, num_hidden_layers=32, num_attention_heads=32, num_key_value_heads=8,
                        intermediate_size=14336, vocab_size=128256, max_position_embeddings=4096), 128, 256
 
@@ -786,8 +791,58 @@ def gpu_busy_ms_per_token(run, n):
     return (full - one) / n / 1e3, (full_sum - one_sum) / n / 1e3
 
 
+def checkpoint_v3_record(model, setup, prompt, uncompressed, device):
+    """save_pretrained of the compressed model (its weights materialized
+    from the GPU, storage v2 encoded on the host) and from_pretrained of the
+    v3 checkpoint (decoded on the host, exported and attached again). The
+    reloaded weights must equal the uncompressed model's bit for bit, and
+    its first-step logits must equal those of the uncompressed weights in a
+    model built the way from_pretrained builds one (on the host, then moved
+    to the GPU: non-persistent buffers such as rotary frequencies are
+    computed there, not stored)."""
+    import tempfile
+
+    from transformers import AutoModelForCausalLM
+
+    from neuralzip_b200 import neuralzip
+
+    neuralzip(setup, device=device)
+    with tempfile.TemporaryDirectory() as folder:
+        t0 = time.perf_counter()
+        model.save_pretrained(folder)
+        save_s = time.perf_counter() - t0
+        stored = model.neuralzip_stats
+        size = sum(f.stat().st_size for f in Path(folder).iterdir())
+        t0 = time.perf_counter()
+        loaded = AutoModelForCausalLM.from_pretrained(folder, attn_implementation="eager")
+        torch.cuda.synchronize(device)
+        load_s = time.perf_counter() - t0
+    original = uncompressed.state_dict()
+    weights_identical = all(torch.equal(w.view(torch.uint8), original[name].cpu().view(torch.uint8))
+                            for name, w in loaded.neuralzip_runtime.materialized_weights())
+    stats = loaded.neuralzip_stats
+    with torch.no_grad():
+        logits = loaded(prompt, use_cache=False).logits.float().cpu()
+        reference = AutoModelForCausalLM.from_config(uncompressed.config, dtype=torch.bfloat16).eval()
+        reference.load_state_dict({k: v.cpu() for k, v in original.items()})
+        reference.to(device)
+        want = reference(prompt, use_cache=False).logits.float().cpu()
+    identical = bool(torch.equal(logits.view(torch.int32), want.view(torch.int32)))
+    del loaded, reference
+    if not (weights_identical and identical):
+        raise AssertionError(f"v3 reload differs: weights {weights_identical}, logits {identical}")
+    return {"save_s": round(save_s, 2), "load_s": round(load_s, 2), "checkpoint_bytes": size,
+            "storage_ratio": round(stored.compression_ratio, 4),
+            "decoding_seconds": round(stats.decoding_seconds, 3),
+            "runtime_encoding_seconds": round(stats.runtime_encoding_seconds, 3),
+            "weights_bitwise": weights_identical, "first_step_logits_bitwise": identical,
+            "what": "save_pretrained (GPU materialize + host storage encode + safetensors write), then "
+                    "from_pretrained (host storage decode + model build + GPU export + attach); logits "
+                    "compared with the uncompressed weights in a model built the same way"}
+
+
 def generation_record(workload, device, *, batch=1, new_tokens=None, reps=3, overlap=True, prefetch_depth=2,
-                      blocks_per_launch=0, tp=None, busy_tokens=16):
+                      blocks_per_launch=0, tp=None, busy_tokens=16, v3=False, layers=None):
     """Random-init model of the config's architecture (N(0, 0.02), norms 1),
     compressed through neuralzip.setup + the GPU export, then greedy
     generation with KV cache and eager attention. An uncompressed copy of
@@ -804,11 +859,25 @@ def generation_record(workload, device, *, batch=1, new_tokens=None, reps=3, ove
 
     torch.cuda.set_device(device)
     config, prompt_len, default_tokens = _model_config(workload)
+    if layers:
+        config.num_hidden_layers = int(layers)
     new_tokens = new_tokens or default_tokens
     config._attn_implementation = "eager"  # the reference's GPU protocol (eager attention)
     torch.manual_seed(0)
-    with torch.device(device):
-        model = AutoModelForCausalLM.from_config(config, dtype=torch.bfloat16).eval()
+    if workload == "config5b":  # each rank builds only its slices (and its replicated parts)
+        from transformers import LlamaForCausalLM
+
+        from neuralzip_b200.gpu.tp import build_tensor_parallel
+
+        rank, world = tp if tp is not None else (0, 1)
+        model, _hooks = build_tensor_parallel(LlamaForCausalLM, config, rank, world, dtype=torch.bfloat16,
+                                              device=device)
+        tp = None  # already sliced
+        sliced = True
+    else:
+        sliced = False
+        with torch.device(device):
+            model = AutoModelForCausalLM.from_config(config, dtype=torch.bfloat16).eval()
     prompt = torch.randint(config.vocab_size, (batch, prompt_len),
                            generator=torch.Generator().manual_seed(1)).to(device)
 
@@ -865,7 +934,7 @@ def generation_record(workload, device, *, batch=1, new_tokens=None, reps=3, ove
     tokens_identical = bool(torch.equal(tokens, ref_tokens))
     busy = {}
     log("generation: GPU-busy (torch.profiler)")
-    for name, m in (("uncompressed", uncompressed), ("compressed", model)):
+    for name, m in (() if sliced else (("uncompressed", uncompressed), ("compressed", model))):
         try:
             union, total = gpu_busy_ms_per_token(runner(m), busy_tokens)
             busy[name] = {"busy_ms_per_token": round(union, 3), "kernel_sum_ms_per_token": round(total, 3)}
@@ -883,6 +952,7 @@ def generation_record(workload, device, *, batch=1, new_tokens=None, reps=3, ove
         torch.cuda.synchronize(device)
         decode_ms.append(a.elapsed_time(b))
     runtime.check_status()
+    checkpoint = checkpoint_v3_record(model, setup, prompt, uncompressed, device) if v3 else None
     decoded = sum(g.encoded.numel * g.encoded.dtype.element_size for g in exported.groups)
     ref_s, comp_s = statistics.median(ref_times), statistics.median(comp_times)
     record = {
@@ -900,6 +970,8 @@ def generation_record(workload, device, *, batch=1, new_tokens=None, reps=3, ove
         "timing": "(t(new_tokens) - t(1)) / (new_tokens - 1): prefill excluded; "
                   f"median of {reps} runs alternating with the uncompressed model",
     }
+    if checkpoint is not None:
+        record["checkpoint_v3"] = checkpoint
     if not (tokens_identical and identical):
         raise AssertionError(f"compressed generation differs from the uncompressed model: {record}")
     del runtime, model, uncompressed
@@ -908,13 +980,13 @@ def generation_record(workload, device, *, batch=1, new_tokens=None, reps=3, ove
 
 
 def run_generation(args, world, rank, local):
-    """--workload config3|config4: the generation record as its own line."""
+    """--workload config3|config4|config5b: the generation record as its own line."""
     device = torch.device("cuda", local)
-    tp = (rank, world) if args.tp and world > 1 else None
+    tp = (rank, world) if (args.tp or args.workload == "config5b") and world > 1 else None
     record, tokens, ref_s, comp_s = generation_record(
         args.workload, device, batch=args.batch, new_tokens=args.new_tokens, reps=args.gen_reps,
         overlap=not args.no_overlap, prefetch_depth=args.prefetch_depth,
-        blocks_per_launch=args.blocks_per_launch, tp=tp)
+        blocks_per_launch=args.blocks_per_launch, tp=tp, layers=args.layers)
     if tp is not None:
         from neuralzip_b200.gpu.tp import assert_same_on_all_ranks
 
@@ -1062,7 +1134,8 @@ def main():
                     "per_dtype": m5["per_dtype"], "config": m5["config"],
                     "note": "one GPU's share of the multi-GPU workload (what each rank decodes under torchrun)"}
             if not args.no_generation:
-                record, *_ = generation_record("config3", device)
+                log("generation: config3")
+                record, *_ = generation_record("config3", device, v3=True)
                 extras["generation"] = record
         else:
             m = config5a_record(args, world, rank, device, clocks, host_threads, args.layers_per_gpu)

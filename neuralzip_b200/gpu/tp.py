@@ -88,6 +88,48 @@ def shard_for_tensor_parallel(model, rank, world, group=None):
     return handles
 
 
+def local_config(config, world):
+    """The config of one rank's slice under `world`-way tensor parallelism:
+    query heads, key/value heads and the MLP width divided by the world
+    size, the head size kept (so o_proj reads heads x head_dim inputs)."""
+    import copy
+
+    for name in ("num_attention_heads", "num_key_value_heads", "intermediate_size"):
+        if getattr(config, name) % world:
+            raise ValueError(f"config.{name} = {getattr(config, name)} does not divide over {world} ranks.")
+    local = copy.deepcopy(config)
+    local.head_dim = getattr(config, "head_dim", None) or config.hidden_size // config.num_attention_heads
+    local.num_attention_heads = config.num_attention_heads // world
+    local.num_key_value_heads = config.num_key_value_heads // world
+    local.intermediate_size = config.intermediate_size // world
+    return local
+
+
+def build_tensor_parallel(model_class, config, rank, world, *, dtype, device, seed=0, std=0.02, group=None):
+    """This rank's slice of a `model_class(config)` built directly, without
+    the full model: a model of the per-rank config (the shapes of a rank's
+    q/k/v/gate/up rows and o/down columns) whose replicated parts
+    (embeddings, norms, LM head) come from `seed` on every rank, and whose
+    sliced projections are drawn N(0, std) from a seed of their own per
+    (rank, layer, projection), with the all-reduce after each row-parallel
+    projection. Returns (model, hook handles)."""
+    torch.manual_seed(seed)
+    with torch.device(device):
+        model = model_class(local_config(config, world)).to(dtype).eval()
+    handles = []
+    with torch.no_grad():
+        for index, layer in enumerate(decoder_layers(model)):
+            for k, name in enumerate(_COLUMN + _ROW):
+                linear = layer.get_submodule(name)
+                g = torch.Generator(device=linear.weight.device).manual_seed(
+                    (seed * 1_000_003 + rank) * 1_000_003 + index * 16 + k)
+                linear.weight.copy_(torch.randn(linear.weight.shape, generator=g, device=linear.weight.device) * std)
+            if world > 1:
+                for name in _ROW:
+                    handles.append(layer.get_submodule(name).register_forward_hook(_all_reduce_hook(group)))
+    return model, handles
+
+
 def assert_same_on_all_ranks(tensor, group=None):
     """Raises unless `tensor` is bit-identical on every rank (a cheap
     all-gather of its bytes)."""

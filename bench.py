@@ -796,36 +796,37 @@ def checkpoint_v3_record(model, setup, prompt, uncompressed, device):
     from the GPU, storage v2 encoded on the host) and from_pretrained of the
     v3 checkpoint (decoded on the host, exported and attached again). The
     reloaded weights must equal the uncompressed model's bit for bit, and
-    its first-step logits must equal those of the uncompressed weights in a
-    model built the way from_pretrained builds one (on the host, then moved
-    to the GPU: non-persistent buffers such as rotary frequencies are
-    computed there, not stored)."""
+    its first-step logits must equal those of the same weights loaded by
+    Transformers' own from_pretrained from an ordinary checkpoint (both
+    loads with the same dtype and attention, so both models are built the
+    same way)."""
     import tempfile
 
-    from transformers import AutoModelForCausalLM
-
     from neuralzip_b200 import neuralzip
+    from neuralzip_b200.gpu import pretrained
 
     neuralzip(setup, device=device)
+    cls = type(uncompressed)
+    options = {"dtype": torch.bfloat16, "attn_implementation": "eager"}
     with tempfile.TemporaryDirectory() as folder:
+        compressed_dir, plain_dir = Path(folder) / "v3", Path(folder) / "plain"
         t0 = time.perf_counter()
-        model.save_pretrained(folder)
+        model.save_pretrained(compressed_dir)
         save_s = time.perf_counter() - t0
         stored = model.neuralzip_stats
-        size = sum(f.stat().st_size for f in Path(folder).iterdir())
+        size = sum(f.stat().st_size for f in compressed_dir.iterdir())
         t0 = time.perf_counter()
-        loaded = AutoModelForCausalLM.from_pretrained(folder, attn_implementation="eager")
+        loaded = cls.from_pretrained(compressed_dir, **options)
         torch.cuda.synchronize(device)
         load_s = time.perf_counter() - t0
+        pretrained._ORIGINAL["save"](uncompressed, plain_dir)
+        reference = pretrained._ORIGINAL["load"](cls, plain_dir, **options).to(device).eval()
     original = uncompressed.state_dict()
     weights_identical = all(torch.equal(w.view(torch.uint8), original[name].cpu().view(torch.uint8))
                             for name, w in loaded.neuralzip_runtime.materialized_weights())
     stats = loaded.neuralzip_stats
     with torch.no_grad():
         logits = loaded(prompt, use_cache=False).logits.float().cpu()
-        reference = AutoModelForCausalLM.from_config(uncompressed.config, dtype=torch.bfloat16).eval()
-        reference.load_state_dict({k: v.cpu() for k, v in original.items()})
-        reference.to(device)
         want = reference(prompt, use_cache=False).logits.float().cpu()
     identical = bool(torch.equal(logits.view(torch.int32), want.view(torch.int32)))
     del loaded, reference
@@ -838,7 +839,7 @@ def checkpoint_v3_record(model, setup, prompt, uncompressed, device):
             "weights_bitwise": weights_identical, "first_step_logits_bitwise": identical,
             "what": "save_pretrained (GPU materialize + host storage encode + safetensors write), then "
                     "from_pretrained (host storage decode + model build + GPU export + attach); logits "
-                    "compared with the uncompressed weights in a model built the same way"}
+                    "compared with the same weights loaded by Transformers from an ordinary checkpoint"}
 
 
 def generation_record(workload, device, *, batch=1, new_tokens=None, reps=3, overlap=True, prefetch_depth=2,

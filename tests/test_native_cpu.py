@@ -290,3 +290,59 @@ def test_native_clustering_matches_sequential_rule(share):
     assert len(centroids) == len(cls) and np.allclose(centroids, np.stack(cent), rtol=0, atol=1e-12)
     if not share:
         assert len(cls) == n
+
+
+def _gaussian_checkpoint():
+    g = torch.Generator().manual_seed(9)
+    named = {"a": (torch.randn(64, 4096, generator=g) * 0.02).to(torch.bfloat16),
+             "b": (torch.randn(40, 1000, generator=g) * 0.5).to(torch.float16),
+             "c": torch.randn(33, 517, generator=g) * 0.1}
+    setup = NeuralZipSetup(chunk_size=8192).build(named)
+    blob, metadata, _sizes, _seconds = NeuralZipCompressor(setup, threads=2).encode(named.items())
+    return named, setup, blob, metadata
+
+
+def test_native_storage_decode_matches_the_per_chunk_wrapper():
+    """The one-call storage decode (nz_storage_decode) and the per-lane
+    chunk-list wrapper (huff0.decompress_mixed_streams_many, the reference's
+    decode-queue signature) give the original bytes for singleton, mixed and
+    raw chunks of bf16, fp16 and fp32 tensors."""
+    from neuralzip_b200 import huff0
+    from neuralzip_b200.storage import StorageReader
+
+    named, setup, blob, metadata = _gaussian_checkpoint()
+    modes = {c["mode"] for t in metadata["tensors"] for lane in t["groups"] for c in lane}
+    assert {"raw", "shared_huff0", "mixed_huffman"} <= modes
+    for threads in (1, 3):
+        decoded = NeuralZipCompressor(setup, threads=threads).decode(blob, metadata)
+        assert all(torch.equal(decoded[n].view(torch.uint8), t.view(torch.uint8)) for n, t in named.items())
+    reader = StorageReader(blob, metadata)
+    books = {b.codebook_id: huff0.build_decodebook(b.codebook, vocab=b.vocab) for b in reader.codebooks()}
+    specs = [(t.element_size, t.bit_reorder, t.numel,
+              [[(c.mode, c.payload, c.symbol_count, books.get(c.codebook_id)) for c in lane.chunks]
+               for lane in t.groups]) for t in reader.tensors()]
+    for out, t in zip(huff0.decompress_mixed_streams_many(specs, threads=2), reader.tensors()):
+        assert bytes(out) == named[t.name].reshape(-1).view(torch.uint8).numpy().tobytes()
+
+
+def test_native_storage_decode_reports_corrupt_chunks():
+    """A corrupted coded payload fails the whole call with the decoder's
+    message; inconsistent metadata is rejected before any decoding."""
+    import copy
+
+    named, setup, blob, metadata = _gaussian_checkpoint()
+    coded = next(c for t in metadata["tensors"] for lane in t["groups"] for c in lane if c["mode"] == "shared_huff0")
+    bad = blob.clone()
+    offset, size = coded["payload"]
+    bad[offset + 6:offset + size] = 0xFF  # streams of garbage behind an intact jump table
+    with pytest.raises(ValueError):
+        NeuralZipCompressor(setup).decode(bad, metadata)
+    broken = copy.deepcopy(metadata)
+    raw = next(c for t in broken["tensors"] for lane in t["groups"] for c in lane if c["mode"] == "raw")
+    raw["payload"][1] -= 1
+    with pytest.raises(ValueError, match="Raw payload size mismatch"):
+        NeuralZipCompressor(setup).decode(blob, broken)
+    broken = copy.deepcopy(metadata)
+    broken["tensors"][0]["groups"][0][0]["symbols"] += 1
+    with pytest.raises(ValueError, match="Unaligned chunk boundaries|exceeds"):
+        NeuralZipCompressor(setup).decode(blob, broken)

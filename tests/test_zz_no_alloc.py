@@ -5,8 +5,9 @@ serving process whose memory pool has already reserved all of HBM, or a host
 path that must not call cudaMalloc because cudaMalloc may synchronize the
 device. For them the library keeps the decode's work-queue counters in its
 own device memory, and this entry point uses those instead of a scratch
-buffer from the caller. These tests drive it through the C ABI, twice in a
-row, and compare its output with the regular launch's, bit for bit (integer
+buffer from the caller. These tests drive it through the C ABI, several
+times in a row on a stream of the caller's, with batches of one and of three
+work queues, and compare its output with the regular launch's, bit for bit (integer
 work: the tolerance is zero, as in every other decode test).
 
 The file is named to be collected last, so that a run stopping at the
@@ -77,16 +78,27 @@ def test_noalloc_launch_matches_regular_launch():
     for out, raw in zip(expected, raws):
         assert bytes(out.cpu().view(torch.uint8).numpy()) == raw
 
-    # Two allocation-free launches in a row: the second one finds the
-    # library's counters set back to zero by the first.
-    for _ in range(2):
-        for out in outs:
-            out.view(torch.int16).fill_(-1)
-        _native.decode_launch_noalloc(batch.launch, stream.cuda_stream)
-        torch.cuda.synchronize()
-        decoder.check_status(batch)
-        for out, ref in zip(outs, expected):
-            assert torch.equal(out.view(torch.int16), ref.view(torch.int16))
+    # Allocation-free launches on a stream of the caller's own (the first
+    # one in the process also sets up the library's counters), alternating
+    # between a one-queue batch and the three-queue batch: each launch finds
+    # every counter it uses, including the finished-CTA count at index
+    # `queues`, set back to zero by the launch before it.
+    single = decoder.prepare_batch(groups[:1])
+    assert single.launch.queues == 1
+    side = torch.cuda.Stream()
+    side.wait_stream(stream)
+    with torch.cuda.stream(side):
+        for current in (single, batch, single, batch):
+            for out in outs:
+                out.view(torch.int16).fill_(-1)
+            _native.decode_launch_noalloc(current.launch, side.cuda_stream)
+            side.synchronize()
+            decoder.check_status(current)
+            decoded = outs[:1] if current is single else outs
+            for out, ref in zip(decoded, expected):
+                assert torch.equal(out.view(torch.int16), ref.view(torch.int16))
+            for out in outs[len(decoded):]:
+                assert bool((out.view(torch.int16) == -1).all())
 
 
 def test_noalloc_launch_rejects_too_many_queues():

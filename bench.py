@@ -357,6 +357,44 @@ def time_launches(fn, stream, launches, reps=5):
     return statistics.median(out)
 
 
+def copy_bound(host, stream, reps=3):
+    """The host links' bound on a host-to-host decode: the same bytes
+    copied with no decode, H2D alone (compressed arena), D2H alone (decoded
+    workspaces) and both at once on the HostDecoder's two copy streams;
+    median ms of `reps` each."""
+    rt = host.runtime
+
+    def h2d():
+        with torch.cuda.stream(host.h2d):
+            rt.arena.copy_(host.host_arena, non_blocking=True)
+
+    def d2h():
+        with torch.cuda.stream(host.d2h):
+            for dtype, out in host.host_outputs.items():
+                out.copy_(rt.workspaces[dtype], non_blocking=True)
+
+    def timed(copies):
+        out = []
+        for _ in range(reps):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            for s in (host.h2d, host.d2h):
+                s.wait_event(a)
+            for copy in copies:
+                copy()
+            for s in (host.h2d, host.d2h):
+                stream.wait_stream(s)
+            b.record(stream)
+            torch.cuda.synchronize()
+            out.append(a.elapsed_time(b))
+        return statistics.median(out)
+
+    h2d_ms, d2h_ms, both_ms = timed((h2d,)), timed((d2h,)), timed((h2d, d2h))
+    return {"h2d_ms": round(h2d_ms, 3), "h2d_gbs": round(host.h2d_bytes / h2d_ms / 1e6, 2),
+            "d2h_ms": round(d2h_ms, 3), "d2h_gbs": round(host.d2h_bytes / d2h_ms / 1e6, 2),
+            "both_ms": round(both_ms, 3)}
+
+
 def stored_traffic(elements):
     """DRAM bytes of one bf16 launch from the committed ncu capture of the
     full config-2 launch, scaled to `elements` (traffic grows in proportion
@@ -503,9 +541,14 @@ def measure_bulk(named, export, args, world, device, clocks):
         for name, tensor in named.items():
             if not torch.equal(decoded[name].reshape(-1).view(torch.uint8), tensor.reshape(-1).view(torch.uint8)):
                 raise AssertionError(f"e2e decode of {name} is not bit-exact")
+        links = copy_bound(host, stream)
+        links["frac"] = round(links["both_ms"] / e_ms, 4)
+        links["what"] = ("the step's H2D and D2H bytes copied with no decode, alone and both at once on the "
+                         "same streams; frac = both_ms / e2e ms_per_step (1.0: the decode hides entirely "
+                         "behind the host copies)")
         e2e = {"value": round(decoded_bytes * world / (e_ms * 1e-3) / 1e9, 3), "unit": "GB/s",
                "h2d_bytes_per_step": host.h2d_bytes, "d2h_bytes_per_step": host.d2h_bytes,
-               "ms_per_step": round(e_ms, 3),
+               "ms_per_step": round(e_ms, 3), "copy_bound": links,
                "path": f"HostDecoder: pinned host arena -> H2D -> tile decode -> D2H of every decoded weight, "
                        f"{len(host.pieces)} pieces pipelined on three streams"}
         del host

@@ -83,9 +83,10 @@ def parse_args():
     p.add_argument("--no-generation", action="store_true")
     p.add_argument("--no-config5a", action="store_true", help="N=1: skip the one-GPU share of config 5a")
     p.add_argument("--e2e-pieces", type=int, default=16, help="pipeline pieces of the host-to-host decode")
-    p.add_argument("--workload", choices=("bulk", "config3", "config4", "config5b"), default="bulk",
-                   help="bulk: config 2 at N=1, config 5a under torchrun (default line); config3/4: generation; "
-                        "config5b: tensor-parallel generation over the torchrun ranks, each building its slices")
+    p.add_argument("--workload", choices=("bulk", "config1", "config3", "config4", "config5b"), default="bulk",
+                   help="bulk: config 2 at N=1, config 5a under torchrun (default line); config1: the single-tensor "
+                        "singleton record alone; config3/4: generation; config5b: tensor-parallel generation over "
+                        "the torchrun ranks, each building its slices")
     p.add_argument("--layers", type=int, default=None, help="config5b: decoder layers (80 in configs[4])")
     p.add_argument("--new-tokens", type=int, default=None)
     p.add_argument("--no-overlap", action="store_true", help="sequential decode schedule")
@@ -719,9 +720,14 @@ def config1_record(device, clocks, copies=16, seconds=3.0):
     with torch.cuda.graph(graph):
         for b in batches:
             decoder.decode_batch(b)
-    for _ in range(3):
-        graph.replay()
-    torch.cuda.synchronize(device)
+    # Warm-up by time, not count: run alone (--workload config1) this is
+    # the process's first GPU work, and a few replays leave the per-launch
+    # time at twice its steady value.
+    t_warm = time.perf_counter()
+    while time.perf_counter() - t_warm < 0.5:
+        for _ in range(10):
+            graph.replay()
+        torch.cuda.synchronize(device)
     with clocks.timed():
         per_launch_ms = time_launches(graph.replay, stream, 10) / copies
     log("config1: batched launch")
@@ -1046,6 +1052,19 @@ def run_generation(args, world, rank, local):
             **record}))
 
 
+def run_config1(local):
+    """--workload config1: the config-1 record (one 4096x4096 bf16 tensor,
+    singleton codebooks) as its own line, on one GPU."""
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    with NvmlClocks(device.index) as clocks:
+        record = config1_record(device, clocks)
+    print(json.dumps({
+        "metric": "decoded weight GB/s (config 1, one decode per launch)",
+        "value": record["per_launch"]["decoded_gbs"], "unit": "GB/s", "n_gpus": 1, "higher_is_better": True,
+        "clocks": clocks.summary(), **record}))
+
+
 # ---- --impl reference -------------------------------------------------------------
 
 def run_reference(args, world, rank):
@@ -1131,7 +1150,9 @@ def main():
     args = parse_args()
     world, rank, local = dist_setup()
     if args.workload != "bulk" or args.impl == "reference":
-        if args.workload != "bulk":
+        if args.workload == "config1":
+            run_config1(local)
+        elif args.workload != "bulk":
             run_generation(args, world, rank, local)
         else:
             run_reference(args, world, rank)

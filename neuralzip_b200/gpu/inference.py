@@ -506,9 +506,17 @@ if hasattr(torch._C, "_cuda_getCurrentRawStream"):
     _current_stream_handle = torch._C._cuda_getCurrentRawStream  # noqa: F811  (same value, no Stream object)
 
 
+# "auto" launch units decode at least this many bytes where blocks are
+# smaller: a launch of one small layer (tens of MB) is a single wave of tiles
+# whose time is the tiles' serial decode latency, while a few such layers in
+# one launch keep every warp busy with several tiles.
+AUTO_UNIT_BYTES = 128 << 20
+
+
 def _plan_units(exported, blocks_per_launch):
     """Consecutive blocks decoded by one launch: fixed-size runs, or with
-    "auto" greedy runs whose decoded bytes stay within the largest block's."""
+    "auto" greedy runs whose decoded bytes stay within the largest block's
+    or AUTO_UNIT_BYTES, whichever is larger."""
     blocks = exported.block_order
     if blocks_per_launch != "auto":
         per_unit = max(1, int(blocks_per_launch))
@@ -516,7 +524,7 @@ def _plan_units(exported, blocks_per_launch):
     size = defaultdict(int)
     for group in exported.groups:
         size[group.block_name] += group.encoded.numel * group.encoded.dtype.element_size
-    limit = max(size.values(), default=0)
+    limit = max(max(size.values(), default=0), AUTO_UNIT_BYTES)
     units, current, total = [], [], 0
     for name in blocks:
         if current and total + size[name] > limit:
@@ -534,8 +542,9 @@ class NeuralZipRuntime:
 
     Blocks are decoded in units of consecutive blocks: ``blocks_per_launch``
     blocks (1 decodes block by block as the reference does), or with "auto"
-    (the default) as many as fit in the size of the largest block, so the
-    workspace is no larger than with single blocks. One launch per dtype
+    (the default) as many as fit in the size of the largest block or in
+    AUTO_UNIT_BYTES (128 MiB) if that is larger, so the workspace is no
+    larger than with single blocks or than 128 MiB a slot. One launch per dtype
     covers a unit, and the blocks of a unit lie side by side in one
     workspace slot. Fewer, larger launches cost less host time per token and
     lose less to the start and end of each launch.

@@ -57,3 +57,34 @@ def test_costlier_tiles_get_more_ctas(weight_layout):
     # fp16 and fp32 tiles weigh twice a bf16 tile: equal tile counts, twice the CTAs.
     nw, ctas = _plan({(BF16, 0): 14800, (weight_layout, 1): 14800})
     assert abs(ctas[(weight_layout, 1)] - 2 * ctas[(BF16, 0)]) <= 2
+
+
+def _export(block_bytes):
+    """A stand-in export: one bf16 group per block with `bytes` of output."""
+    from types import SimpleNamespace
+
+    groups = [SimpleNamespace(block_name=name, encoded=SimpleNamespace(numel=size // 2,
+                                                                       dtype=SimpleNamespace(element_size=2)))
+              for name, size in block_bytes.items()]
+    return SimpleNamespace(block_order=tuple(block_bytes), groups=groups)
+
+
+def test_auto_units_fill_small_blocks_up_to_the_floor():
+    from neuralzip_b200.gpu.inference import AUTO_UNIT_BYTES, _plan_units
+
+    layer = 30 << 20  # a Qwen2.5-0.5B decoder layer: 4 fit in 128 MiB
+    export = _export({f"layers.{i}": layer for i in range(24)})
+    units = _plan_units(export, "auto")
+    assert [len(u) for u in units] == [4] * 6 and AUTO_UNIT_BYTES == 128 << 20
+    assert [b for u in units for b in u] == list(export.block_order)
+
+
+def test_auto_units_keep_the_largest_block_as_the_limit_when_larger():
+    from neuralzip_b200.gpu.inference import _plan_units
+
+    # Llama-3-8B: 436 MB layers and a 1.05 GB LM head: two layers a unit.
+    blocks = {f"layers.{i}": 436 << 20 for i in range(4)}
+    blocks["lm_head"] = 1050 << 20
+    units = _plan_units(_export(blocks), "auto")
+    assert units == [("layers.0", "layers.1"), ("layers.2", "layers.3"), ("lm_head",)]
+    assert _plan_units(_export(blocks), 1) == [(b,) for b in blocks]

@@ -350,12 +350,15 @@ struct MergeGroup {
 };
 
 // The works [begin, end) of one CTA, taken in turn by its NW warps, for
-// one element layout. `table` is the CTA's staged decode table.
+// one element layout. `table` is the CTA's decode table; while `table_bar`
+// (the shared address of its copy's mbarrier, 0 when the CTA has no table)
+// is nonzero the copy may still be in flight, and each warp waits for it
+// just before its first lookup.
 template <int ES, bool REORDER, int NW, bool kQueue>
 __device__ __forceinline__ void decode_works(const nz_group* __restrict__ groups,
                                              const nz_work* __restrict__ works, uint32_t begin,
                                              uint32_t end, const uint32_t* __restrict__ table,
-                                             uint32_t* stage, int32_t* __restrict__ status,
+                                             uint32_t table_bar, uint32_t* stage, int32_t* __restrict__ status,
                                              uint32_t* __restrict__ queue) {
     constexpr uint32_t kBitBufWords = bit_buf_words(NW);
     using L = Layout<ES, REORDER>;
@@ -364,6 +367,17 @@ __device__ __forceinline__ void decode_works(const nz_group* __restrict__ groups
     const uint32_t warp = threadIdx.x >> 5;
     const uint32_t lane = threadIdx.x & 31U;
     const uint2* table2 = reinterpret_cast<const uint2*>(table);
+    // The warp's first coded tile waits for the table (every lane, and
+    // the warp agrees on the outcome). A copy that did not arrive within
+    // the bounded wait sets status 5, and the warp decodes nothing more.
+    bool table_pending = table_bar != 0U;
+    auto table_arrived = [&]() {
+        if (!table_pending) return true;
+        table_pending = false;
+        if (__all_sync(0xFFFFFFFFU, mbar_wait(table_bar, 0U))) return true;
+        if (lane == 0 && status) *status = kStatusCopyTimeout;
+        return false;
+    };
     // Without a queue the warps take the CTA's works in turn. With one, each
     // warp claims the next work of the range shared by the queue's CTAs
     // (lane 0, one atomic per work), the next claim issued halfway through
@@ -567,10 +581,12 @@ __device__ __forceinline__ void decode_works(const nz_group* __restrict__ groups
                 }
                 asm volatile("cp.async.wait_all;" ::: "memory");
                 __syncwarp();
+                if (!table_arrived()) return;
                 Window<true> win;
                 win.init(sbuf - 4U * wa, nullptr, bit0 + incl - len);
                 rounds(win);
             } else {
+                if (!table_arrived()) return;
                 Window<false> win;
                 win.init(0U, gbits, bit0 + incl - len);
                 rounds(win);
@@ -605,12 +621,15 @@ __global__ void __launch_bounds__(NW * 32, ctas_per_sm(NW))
     const bool bad_queue = kQueue && cta.queue >= queues;
     uint32_t* queue = kQueue && !bad_queue ? scratch + cta.queue : nullptr;
     // The decode table (its leading table words, rounded up to 16 bytes)
-    // arrives by one bulk copy issued by thread 0. A copy that does not
-    // complete within the bounded wait sets status 5, and after a second
-    // bounded wait for it the CTA decodes nothing.
-    bool table_ok = true;
+    // arrives by one bulk copy issued by thread 0. The warps do not wait for
+    // it here: each claims its first tile, reads its records and copies its
+    // bitstream while the table is in flight, and waits for the table just
+    // before its first lookup. Thread 0 waits for the copy (bounded) before
+    // the CTA ends, so that no copy into this CTA's shared memory outlives
+    // it; a copy that never arrives sets status 5.
+    uint32_t bar = 0;
     if (cta.lut != NZ_RAW_LUT) {
-        const uint32_t bar = static_cast<uint32_t>(__cvta_generic_to_shared(smem + NZ_LUT_WORDS + NW * warp_words(NW)));
+        bar = static_cast<uint32_t>(__cvta_generic_to_shared(smem + NZ_LUT_WORDS + NW * warp_words(NW)));
         if (threadIdx.x == 0) mbar_init(bar);
         __syncthreads();
         if (threadIdx.x == 0) {
@@ -618,26 +637,21 @@ __global__ void __launch_bounds__(NW * 32, ctas_per_sm(NW))
             bulk_load(static_cast<uint32_t>(__cvta_generic_to_shared(table)),
                       reinterpret_cast<const void*>(luts[cta.lut]), n4 * 16U, bar);
         }
-        table_ok = mbar_wait(bar, 0U);
-        if (!table_ok) {
-            if (threadIdx.x == 0 && status) *status = kStatusCopyTimeout;
-            mbar_wait(bar, 0U);
-        }
     }
-    __syncthreads();
-    switch (bad_queue || !table_ok ? 0xFFFFU : cta.layout) {
+    switch (bad_queue ? 0xFFFFU : cta.layout) {
         case NZ_LAYOUT_BF16:
-            decode_works<2, true, NW, kQueue>(groups, works, cta.begin, cta.end, table, stage, status, queue);
+            decode_works<2, true, NW, kQueue>(groups, works, cta.begin, cta.end, table, bar, stage, status, queue);
             break;
         case NZ_LAYOUT_FP16:
-            decode_works<2, false, NW, kQueue>(groups, works, cta.begin, cta.end, table, stage, status, queue);
+            decode_works<2, false, NW, kQueue>(groups, works, cta.begin, cta.end, table, bar, stage, status, queue);
             break;
         case NZ_LAYOUT_FP32:
-            decode_works<4, true, NW, kQueue>(groups, works, cta.begin, cta.end, table, stage, status, queue);
+            decode_works<4, true, NW, kQueue>(groups, works, cta.begin, cta.end, table, bar, stage, status, queue);
             break;
         default:
-            if (threadIdx.x == 0 && status && table_ok) *status = bad_queue ? kStatusBadQueue : kStatusBadLayout;
+            if (threadIdx.x == 0 && status) *status = bad_queue ? kStatusBadQueue : kStatusBadLayout;
     }
+    if (bar && threadIdx.x == 0 && !mbar_wait(bar, 0U) && status) *status = kStatusCopyTimeout;
     if constexpr (kQueue) {
         // The launch's last CTA to finish sets the queue counters back to
         // zero for the next launch that uses this scratch.

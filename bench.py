@@ -1109,7 +1109,9 @@ def run_reference(args, world, rank):
         "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(mean * 1e3, 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "u8", "data": "synthetic",
-        "config": {"workload": workload, "chunks": len(chunks), "threads": threads},
+        "config": {"workload": workload, "chunks": len(chunks), "threads": threads,
+                   "untimed": "codebooks chosen by this build's NeuralZipSetup (the reference's setup decisions) "
+                              "and chunks encoded by the reference's own encoder, before the timed decode"},
         "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": "reference",
                          "cpu_model": cpu_model(), "sample": sample},
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},

@@ -510,7 +510,7 @@ if hasattr(torch._C, "_cuda_getCurrentRawStream"):
 # smaller: a launch of one small layer (tens of MB) is a single wave of tiles
 # whose time is the tiles' serial decode latency, while a few such layers in
 # one launch keep every warp busy with several tiles.
-AUTO_UNIT_BYTES = 128 << 20
+AUTO_UNIT_BYTES = 256 << 20
 
 
 def _plan_units(exported, blocks_per_launch):
@@ -543,8 +543,8 @@ class NeuralZipRuntime:
     Blocks are decoded in units of consecutive blocks: ``blocks_per_launch``
     blocks (1 decodes block by block as the reference does), or with "auto"
     (the default) as many as fit in the size of the largest block or in
-    AUTO_UNIT_BYTES (128 MiB) if that is larger, so the workspace is no
-    larger than with single blocks or than 128 MiB a slot. One launch per dtype
+    AUTO_UNIT_BYTES (256 MiB) if that is larger, so the workspace is no
+    larger than with single blocks or than 256 MiB a slot. One launch per dtype
     covers a unit, and the blocks of a unit lie side by side in one
     workspace slot. Fewer, larger launches cost less host time per token and
     lose less to the start and end of each launch.

@@ -72,10 +72,10 @@ def _export(block_bytes):
 def test_auto_units_fill_small_blocks_up_to_the_floor():
     from neuralzip_b200.gpu.inference import AUTO_UNIT_BYTES, _plan_units
 
-    layer = 30 << 20  # a Qwen2.5-0.5B decoder layer: 4 fit in 128 MiB
+    layer = 30 << 20  # a Qwen2.5-0.5B decoder layer: 8 fit in 256 MiB
     export = _export({f"layers.{i}": layer for i in range(24)})
     units = _plan_units(export, "auto")
-    assert [len(u) for u in units] == [4] * 6 and AUTO_UNIT_BYTES == 128 << 20
+    assert [len(u) for u in units] == [8] * 3 and AUTO_UNIT_BYTES == 256 << 20
     assert [b for u in units for b in u] == list(export.block_order)
 
 

@@ -20,7 +20,6 @@ table) can be overridden the way the reference's tests override
 
 from __future__ import annotations
 
-import ctypes
 from dataclasses import dataclass, field
 from pathlib import Path
 

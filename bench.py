@@ -96,6 +96,8 @@ def parse_args():
     p.add_argument("--batch", type=int, default=1, help="generation batch (config 4 also names 8)")
     p.add_argument("--gen-reps", type=int, default=3, help="alternating timed runs per model")
     p.add_argument("--tp", action="store_true", help="generation workloads: tensor parallel over the torchrun ranks")
+    p.add_argument("--cuda-graphs", action="store_true",
+                   help="config3/config4: also time both models with the one-token step captured in a CUDA graph")
     return p.parse_args()
 
 
@@ -891,8 +893,97 @@ def checkpoint_v3_record(model, setup, prompt, uncompressed, device):
                     "compared with the same weights loaded by Transformers from an ordinary checkpoint"}
 
 
+def graph_decode(m, prompt, new_tokens, device, reps):
+    """Greedy decoding of `new_tokens` after `prompt` with a static KV cache
+    and the one-token step captured once in a CUDA graph, so no host work is
+    timed: the prefill runs eagerly (not timed), then every step is one
+    replay (the graph feeds its argmax token and position back to its
+    inputs). Returns the tokens and the ms per token of each rep (CUDA
+    events over the replays). With a compressed model the capture holds the
+    decode launches its forward pre-hooks enqueue, side-stream prefetches
+    included."""
+    from transformers import StaticCache
+
+    batch, plen = prompt.shape
+    stream = torch.cuda.current_stream(device)
+    with torch.no_grad():
+        length = plen + new_tokens + 4
+        cache = StaticCache(config=m.config, max_cache_len=length)
+        first = m(input_ids=prompt, past_key_values=cache, use_cache=True).logits[:, -1].argmax(-1)
+        ids = first[:, None].clone()
+        pos = torch.full((1,), plen, dtype=torch.long, device=device)
+        kv = torch.arange(length, device=device)
+        low = torch.finfo(torch.bfloat16).min
+
+        def step():
+            # Every op is on the device: the position, the causal mask (a 4D
+            # mask is used as given) and the cache slot (each cache layer's
+            # own length counter) advance inside the graph.
+            mask = ((kv > pos).to(torch.bfloat16) * low).view(1, 1, 1, length)
+            nxt = m(input_ids=ids, past_key_values=cache, position_ids=pos.view(1, 1), attention_mask=mask,
+                    use_cache=True).logits[:, -1].argmax(-1)
+            ids.copy_(nxt[:, None])
+            pos.add_(1)
+            return nxt
+
+        def rewind():
+            for layer in cache.layers:
+                layer.cumulative_length.fill_(plen)
+            ids.copy_(first[:, None])
+            pos.fill_(plen)
+
+        # Warm-up on a side stream before the capture (positions the timed
+        # replays rewrite; later positions are masked until written).
+        side = torch.cuda.Stream(device=device)
+        side.wait_stream(stream)
+        with torch.cuda.stream(side):
+            for _ in range(3):
+                step()
+        stream.wait_stream(side)
+        torch.cuda.synchronize(device)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            nxt = step()
+        times, tokens = [], None
+        for _ in range(reps):
+            rewind()
+            steps = []
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            for _ in range(new_tokens - 1):
+                graph.replay()
+                steps.append(nxt.clone())
+            b.record(stream)
+            torch.cuda.synchronize(device)
+            times.append(a.elapsed_time(b) / (new_tokens - 1))
+            tokens = torch.cat([first[:, None], torch.stack(steps, 1)], 1)
+        del graph
+    return tokens, times
+
+
+def graph_record(model, uncompressed, prompt, new_tokens, device, reps):
+    """Both models decoded by graph_decode, alternately; the tokens must be
+    identical (asserted)."""
+    ref_ms, comp_ms = [], []
+    for _ in range(reps):
+        ref_tokens, t = graph_decode(uncompressed, prompt, new_tokens, device, 1)
+        ref_ms += t
+        tokens, t = graph_decode(model, prompt, new_tokens, device, 1)
+        comp_ms += t
+    if not torch.equal(tokens, ref_tokens):
+        raise AssertionError("CUDA-graph generation of the compressed model differs from the uncompressed model")
+    batch = prompt.shape[0]
+    ref, comp = statistics.median(ref_ms), statistics.median(comp_ms)
+    return {"tok_s": round(batch / (comp * 1e-3), 3), "uncompressed_tok_s": round(batch / (ref * 1e-3), 3),
+            "ratio_vs_uncompressed": round(ref / comp, 4), "ms_per_token": round(comp, 3),
+            "uncompressed_ms_per_token": round(ref, 3), "tokens_identical": True,
+            "timing": "static KV cache, the one-token step captured once in a CUDA graph (decode launches and "
+                      f"side-stream prefetches of the compressed model included); CUDA events over {new_tokens - 1} "
+                      f"replays, median of {reps} runs alternating with the uncompressed model"}
+
+
 def generation_record(workload, device, *, batch=1, new_tokens=None, reps=3, overlap=True, prefetch_depth=2,
-                      blocks_per_launch=0, tp=None, busy_tokens=16, v3=False, layers=None):
+                      blocks_per_launch=0, tp=None, busy_tokens=16, v3=False, layers=None, graphs=False):
     """Random-init model of the config's architecture (N(0, 0.02), norms 1),
     compressed through neuralzip.setup + the GPU export, then greedy
     generation with KV cache and eager attention. An uncompressed copy of
@@ -1002,6 +1093,15 @@ def generation_record(workload, device, *, batch=1, new_tokens=None, reps=3, ove
         torch.cuda.synchronize(device)
         decode_ms.append(a.elapsed_time(b))
     runtime.check_status()
+    graph = None
+    if graphs:
+        log("generation: CUDA-graph mode")
+        try:
+            graph = graph_record(model, uncompressed, prompt, new_tokens, device, reps)
+        except AssertionError:
+            raise
+        except Exception as exc:  # a capture the library or Transformers refuses is reported, not hidden
+            graph = {"error": f"{type(exc).__name__}: {exc}"[:300]}
     checkpoint = checkpoint_v3_record(model, setup, prompt, uncompressed, device) if v3 else None
     decoded = sum(g.encoded.numel * g.encoded.dtype.element_size for g in exported.groups)
     ref_s, comp_s = statistics.median(ref_times), statistics.median(comp_times)
@@ -1022,6 +1122,8 @@ def generation_record(workload, device, *, batch=1, new_tokens=None, reps=3, ove
     }
     if checkpoint is not None:
         record["checkpoint_v3"] = checkpoint
+    if graph is not None:
+        record["cuda_graph"] = graph
     if not (tokens_identical and identical):
         raise AssertionError(f"compressed generation differs from the uncompressed model: {record}")
     del runtime, model, uncompressed
@@ -1036,7 +1138,8 @@ def run_generation(args, world, rank, local):
     record, tokens, ref_s, comp_s = generation_record(
         args.workload, device, batch=args.batch, new_tokens=args.new_tokens, reps=args.gen_reps,
         overlap=not args.no_overlap, prefetch_depth=args.prefetch_depth,
-        blocks_per_launch=args.blocks_per_launch, tp=tp, layers=args.layers)
+        blocks_per_launch=args.blocks_per_launch, tp=tp, layers=args.layers,
+        graphs=args.cuda_graphs and tp is None)
     if tp is not None:
         from neuralzip_b200.gpu.tp import assert_same_on_all_ranks
 

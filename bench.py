@@ -893,45 +893,54 @@ def checkpoint_v3_record(model, setup, prompt, uncompressed, device):
                     "compared with the same weights loaded by Transformers from an ordinary checkpoint"}
 
 
+def static_decoder(m, prompt, new_tokens, device):
+    """Greedy decoding of `prompt` with a static KV cache, as graph_decode
+    captures it: the prefill runs (eagerly) here, and returns the first
+    token, `step()` (one token: the model on the current ids with the
+    position, the causal mask and each cache layer's length counter all on
+    the device, its argmax written back to the ids) and `rewind()` (back to
+    the state right after the prefill)."""
+    from transformers import StaticCache
+
+    _batch, plen = prompt.shape
+    length = plen + new_tokens + 4
+    cache = StaticCache(config=m.config, max_cache_len=length)
+    first = m(input_ids=prompt, past_key_values=cache, use_cache=True).logits[:, -1].argmax(-1)
+    ids = first[:, None].clone()
+    pos = torch.full((1,), plen, dtype=torch.long, device=device)
+    kv = torch.arange(length, device=device)
+    low = torch.finfo(torch.bfloat16).min
+
+    def step():
+        # A 4D mask is used as given, so nothing is built on the host.
+        mask = ((kv > pos).to(torch.bfloat16) * low).view(1, 1, 1, length)
+        nxt = m(input_ids=ids, past_key_values=cache, position_ids=pos.view(1, 1), attention_mask=mask,
+                use_cache=True).logits[:, -1].argmax(-1)
+        ids.copy_(nxt[:, None])
+        pos.add_(1)
+        return nxt
+
+    def rewind():
+        for layer in cache.layers:
+            layer.cumulative_length.fill_(plen)
+        ids.copy_(first[:, None])
+        pos.fill_(plen)
+
+    return first, step, rewind
+
+
 def graph_decode(m, prompt, new_tokens, device, reps):
-    """Greedy decoding of `new_tokens` after `prompt` with a static KV cache
-    and the one-token step captured once in a CUDA graph, so no host work is
-    timed: the prefill runs eagerly (not timed), then every step is one
+    """Greedy decoding of `new_tokens` after `prompt` with the one-token
+    step of static_decoder captured once in a CUDA graph, so no host work
+    is timed: the prefill runs eagerly (not timed), then every step is one
     replay (the graph feeds its argmax token and position back to its
     inputs). Returns the tokens and the ms per token of each rep (CUDA
     events over the replays). With a compressed model the capture holds the
     decode launches its forward pre-hooks enqueue, side-stream prefetches
     included."""
-    from transformers import StaticCache
-
-    batch, plen = prompt.shape
     stream = torch.cuda.current_stream(device)
     with torch.no_grad():
-        length = plen + new_tokens + 4
-        cache = StaticCache(config=m.config, max_cache_len=length)
-        first = m(input_ids=prompt, past_key_values=cache, use_cache=True).logits[:, -1].argmax(-1)
-        ids = first[:, None].clone()
-        pos = torch.full((1,), plen, dtype=torch.long, device=device)
-        kv = torch.arange(length, device=device)
-        low = torch.finfo(torch.bfloat16).min
-
-        def step():
-            # Every op is on the device: the position, the causal mask (a 4D
-            # mask is used as given) and the cache slot (each cache layer's
-            # own length counter) advance inside the graph.
-            mask = ((kv > pos).to(torch.bfloat16) * low).view(1, 1, 1, length)
-            nxt = m(input_ids=ids, past_key_values=cache, position_ids=pos.view(1, 1), attention_mask=mask,
-                    use_cache=True).logits[:, -1].argmax(-1)
-            ids.copy_(nxt[:, None])
-            pos.add_(1)
-            return nxt
-
-        def rewind():
-            for layer in cache.layers:
-                layer.cumulative_length.fill_(plen)
-            ids.copy_(first[:, None])
-            pos.fill_(plen)
-
+        first, step, rewind = static_decoder(m, prompt, new_tokens, device)
         # Warm-up on a side stream before the capture (positions the timed
         # replays rewrite; later positions are masked until written).
         side = torch.cuda.Stream(device=device)

@@ -168,7 +168,9 @@ int nz_pack_many(nz_pack_job* jobs, uint64_t count, const nz_dtype* dt,
                  int32_t threads);
 
 /* Raw fragment (no codebook, neuralzip/gpu/inference.py:319-324): applies
- * the reorder and writes every byte lane, the selected one included. */
+ * the reorder and writes every byte lane, the selected one included; a
+ * NULL entry of lanes[] other than the selected lane's skips that lane.
+ * Large inputs are split on the host's threads. */
 int nz_split_lanes(const uint8_t* raw, uint64_t numel, const nz_dtype* dt,
                    uint8_t* const* lanes);
 

@@ -301,14 +301,18 @@ def pack_chunk(codebook, raw, dt):
     return bits[:used.value].copy(), lens, tile_off, lanes, bit_length.value
 
 
-def split_lanes(raw, dt):
-    """Reorders and splits every byte lane (raw fragments)."""
+def split_lanes(raw, dt, selected_only=False):
+    """Reorders and splits every byte lane (raw fragments); with
+    `selected_only`, only the selected lane is written (the others are
+    None)."""
     lib = load()
     raw = np.ascontiguousarray(np.frombuffer(raw, dtype=np.uint8) if isinstance(raw, (bytes, bytearray, memoryview))
                                else raw.reshape(-1).view(np.uint8))
     numel = len(raw) // dt.elem_size
-    lanes = [np.empty(numel, dtype=np.uint8) for _ in range(dt.elem_size)]
-    lane_ptrs = (ctypes.c_void_p * 4)(*[lane.ctypes.data for lane in lanes] + [None] * (4 - len(lanes)))
+    lanes = [np.empty(numel, dtype=np.uint8) if not selected_only or lane == dt.stream_id else None
+             for lane in range(dt.elem_size)]
+    lane_ptrs = (ctypes.c_void_p * 4)(*[None if lane is None else lane.ctypes.data for lane in lanes]
+                                      + [None] * (4 - len(lanes)))
     check(lib.nz_split_lanes(_ptr(raw), numel, ctypes.byref(dt), lane_ptrs))
     return lanes
 

@@ -23,6 +23,7 @@
 #include <exception>
 #include <string>
 #include <thread>
+#include <type_traits>
 #include <vector>
 
 namespace nz {
@@ -319,16 +320,28 @@ inline LaneMasks masks_of(const nz_dtype& dt) {
             ((1U << dt.exp_bits) - 1U) << (dt.mant_bits + 1U)};
 }
 
+// One byte lane of the reordered elements: a loop per lane, with nothing
+// but the element's load, reorder and shift in it, so that it vectorizes.
 template <unsigned E>
-inline uint32_t load_word(const uint8_t* raw, uint64_t index) {
-    uint32_t value = 0;
-    std::memcpy(&value, raw + index * E, E);
-    return value;
-}
-
-inline uint32_t reorder_value(uint32_t value, const nz_dtype& dt, const LaneMasks& m) {
-    if (!dt.reorder) return value;
-    return (value & m.mant) | ((value >> dt.exp_bits) & m.sign) | ((value << 1U) & m.exp);
+void split_one(const uint8_t* __restrict__ raw, uint64_t numel, const nz_dtype& dt, const LaneMasks& m,
+               unsigned lane, uint8_t* __restrict__ out) {
+    const unsigned shift = 8U * lane;
+    if (!dt.reorder) {
+        for (uint64_t i = 0; i < numel; ++i) out[i] = raw[i * E + lane];
+        return;
+    }
+    // Elements are read at their own width (a 2-byte copy into a 32-bit
+    // word does not vectorize).
+    using Word = typename std::conditional<E == 2, uint16_t, uint32_t>::type;
+    const Word mant = static_cast<Word>(m.mant), sign = static_cast<Word>(m.sign), exp = static_cast<Word>(m.exp);
+    const unsigned exp_bits = dt.exp_bits;
+    for (uint64_t i = 0; i < numel; ++i) {
+        Word value;
+        std::memcpy(&value, raw + i * E, E);
+        const Word v = static_cast<Word>((value & mant) | ((value >> exp_bits) & sign) |
+                                         (static_cast<Word>(value << 1U) & exp));
+        out[i] = static_cast<uint8_t>(v >> shift);
+    }
 }
 
 // Extracts the selected lane into `symbols` and the other lanes into
@@ -337,13 +350,9 @@ template <unsigned E>
 void split(const uint8_t* raw, uint64_t numel, const nz_dtype& dt, uint8_t* symbols,
            uint8_t* const* lanes) {
     const LaneMasks m = masks_of(dt);
-    uint8_t* out[4] = {nullptr, nullptr, nullptr, nullptr};
-    for (unsigned lane = 0; lane < E; ++lane)
-        out[lane] = lane == dt.stream_id ? symbols : (lanes ? lanes[lane] : nullptr);
-    for (uint64_t i = 0; i < numel; ++i) {
-        const uint32_t v = reorder_value(load_word<E>(raw, i), dt, m);
-        for (unsigned lane = 0; lane < E; ++lane)
-            if (out[lane]) out[lane][i] = static_cast<uint8_t>(v >> (8U * lane));
+    for (unsigned lane = 0; lane < E; ++lane) {
+        uint8_t* out = lane == dt.stream_id ? symbols : (lanes ? lanes[lane] : nullptr);
+        if (out) split_one<E>(raw, numel, dt, m, lane, out);
     }
 }
 
@@ -610,7 +619,17 @@ int nz_split_lanes(const uint8_t* raw, uint64_t numel, const nz_dtype* dt, uint8
     NZ_GUARD({
         if (!dt || !lanes || (numel && !raw)) throw Error(NZ_EVALUE, "Null argument.");
         nz::check_dtype(*dt);
-        nz::split_lanes(raw, numel, *dt, lanes[dt->stream_id], lanes);
+        if (!lanes[dt->stream_id]) throw Error(NZ_EVALUE, "The selected lane's buffer is null.");
+        // Large inputs are split in blocks on the host's threads.
+        constexpr uint64_t kBlock = uint64_t{1} << 20;
+        const uint64_t blocks = (numel + kBlock - 1) / kBlock;
+        nz::run_jobs(blocks, 0, [&](uint64_t b) {
+            const uint64_t first = b * kBlock, n = std::min<uint64_t>(kBlock, numel - first);
+            uint8_t* part[4] = {nullptr, nullptr, nullptr, nullptr};
+            for (uint32_t lane = 0; lane < dt->elem_size; ++lane)
+                part[lane] = lanes[lane] ? lanes[lane] + first : nullptr;
+            nz::split_lanes(raw + first * dt->elem_size, n, *dt, part[dt->stream_id], part);
+        });
     })
 }
 

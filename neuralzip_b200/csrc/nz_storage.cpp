@@ -378,6 +378,29 @@ void decode_piece(const nz_storage_piece& p) {
 
 }  // namespace nz
 
+namespace {
+
+// Exponent counts of elements [begin, end), four interleaved tables.
+template <typename Word>
+void count_exponents(const uint8_t* raw, uint64_t begin, uint64_t end, uint32_t shift, uint32_t mask,
+                     uint64_t (&local)[4][256]) {
+    auto exponent = [&](uint64_t k) {
+        Word v;
+        std::memcpy(&v, raw + sizeof(Word) * k, sizeof(Word));
+        return (static_cast<uint32_t>(v) >> shift) & mask;
+    };
+    uint64_t i = begin;
+    for (; i + 4 <= end; i += 4) {
+        ++local[0][exponent(i)];
+        ++local[1][exponent(i + 1)];
+        ++local[2][exponent(i + 2)];
+        ++local[3][exponent(i + 3)];
+    }
+    for (; i < end; ++i) ++local[0][exponent(i)];
+}
+
+}  // namespace
+
 extern "C" {
 
 int nz_count_tokens(const uint8_t* data, uint64_t size, const uint8_t* vocab, uint32_t vocab_size,
@@ -391,8 +414,31 @@ int nz_count_tokens(const uint8_t* data, uint64_t size, const uint8_t* vocab, ui
             if (lookup[pair]) throw Error(NZ_EVALUE, "Duplicate mixed pair definition.");
             lookup[pair] = static_cast<uint16_t>(256 + i / 2);
         }
+        if (!vocab_size) {
+            // Plain byte counts: independent blocks on the host's threads,
+            // each into four interleaved local tables, added under a lock.
+            constexpr uint64_t kBlock = uint64_t{1} << 22;
+            std::mutex add;
+            nz::run_jobs((size + kBlock - 1) / kBlock, 0, [&](uint64_t b) {
+                uint64_t local[4][256] = {};
+                const uint8_t* p = data + b * kBlock;
+                const uint64_t n = std::min<uint64_t>(kBlock, size - b * kBlock);
+                uint64_t i = 0;
+                for (; i + 4 <= n; i += 4) {
+                    ++local[0][p[i]];
+                    ++local[1][p[i + 1]];
+                    ++local[2][p[i + 2]];
+                    ++local[3][p[i + 3]];
+                }
+                for (; i < n; ++i) ++local[0][p[i]];
+                std::lock_guard<std::mutex> hold(add);
+                for (uint32_t v = 0; v < 256; ++v) counts[v] += local[0][v] + local[1][v] + local[2][v] + local[3][v];
+            });
+            return NZ_OK;
+        }
+        // The greedy pair parse is sequential (a pair can start anywhere).
         for (uint64_t i = 0; i < size;) {
-            const uint32_t pair = vocab_size && i + 1 < size ? lookup[data[i] | (data[i + 1] << 8)] : 0;
+            const uint32_t pair = i + 1 < size ? lookup[data[i] | (data[i + 1] << 8)] : 0;
             ++counts[pair ? pair : data[i]];
             i += pair ? 2 : 1;
         }
@@ -405,23 +451,19 @@ int nz_exponent_histograms(const uint8_t* raw, uint64_t numel, const nz_dtype* d
         if ((numel && !raw) || !dt || !histograms || step == 0) throw Error(NZ_EVALUE, "Null argument.");
         nz::check_dtype(*dt);
         const uint32_t mask = (1U << dt->exp_bits) - 1U;
-        for (uint64_t begin = 0, chunk = 0; begin < numel; begin += step, ++chunk) {
+        const uint32_t shift = dt->mant_bits;
+        // Chunks are independent rows: they are counted on the host's
+        // threads, each into four interleaved local tables (consecutive
+        // elements rarely wait on the same counter) added into its row.
+        const uint64_t chunks = (numel + step - 1) / step;
+        nz::run_jobs(chunks, 0, [&](uint64_t chunk) {
+            uint64_t local[4][256] = {};
+            const uint64_t begin = chunk * step, end = std::min(numel, begin + step);
+            if (dt->elem_size == 2) count_exponents<uint16_t>(raw, begin, end, shift, mask, local);
+            else count_exponents<uint32_t>(raw, begin, end, shift, mask, local);
             uint64_t* h = histograms + chunk * 256;
-            const uint64_t end = std::min(numel, begin + step);
-            if (dt->elem_size == 2) {
-                for (uint64_t i = begin; i < end; ++i) {
-                    uint16_t v;
-                    std::memcpy(&v, raw + 2 * i, 2);
-                    ++h[(v >> dt->mant_bits) & mask];
-                }
-            } else {
-                for (uint64_t i = begin; i < end; ++i) {
-                    uint32_t v;
-                    std::memcpy(&v, raw + 4 * i, 4);
-                    ++h[(v >> dt->mant_bits) & mask];
-                }
-            }
-        }
+            for (uint32_t b = 0; b < 256; ++b) h[b] += local[0][b] + local[1][b] + local[2][b] + local[3][b];
+        });
     })
 }
 

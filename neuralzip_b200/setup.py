@@ -147,7 +147,7 @@ class NeuralZipSetup:
             spec = DTYPES[tensor.dtype]
             raw = tensor.detach().cpu().contiguous().reshape(-1).view(torch.uint8).numpy()
             dt = _dtype_struct(spec)
-            lane = _native.split_lanes(raw, dt)[spec.gpu_stream]
+            lane = _native.split_lanes(raw, dt, selected_only=True)[spec.gpu_stream]
             step = _stream_chunk_size(self.chunk_size, spec.element_size)
             key = (str(name), spec.name, spec.gpu_stream)
             pooled[key] = _native.count_tokens(lane, b"")

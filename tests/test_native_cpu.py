@@ -15,7 +15,7 @@ from neuralzip_b200 import _native, huff0
 from neuralzip_b200.compressor import NeuralZipCompressor
 from neuralzip_b200.dtypes import DTYPES
 from neuralzip_b200.gpu.inference import GPUCodebook, export_model_for_gpu
-from neuralzip_b200.setup import NeuralZipSetup
+from neuralzip_b200.setup import NeuralZipSetup, _dtype_struct
 from oracle import oracle as O
 
 HEADER = Path(__file__).resolve().parents[1] / "include" / "nz_b200.h"
@@ -346,3 +346,66 @@ def test_native_storage_decode_reports_corrupt_chunks():
     broken["tensors"][0]["groups"][0][0]["symbols"] += 1
     with pytest.raises(ValueError, match="Unaligned chunk boundaries|exceeds"):
         NeuralZipCompressor(setup).decode(blob, broken)
+
+
+def _reordered_words(raw, spec):
+    """numpy restatement of DTypeSpec.reorder_bytes on whole words."""
+    w = raw.view(np.uint16 if spec.element_size == 2 else np.uint32).astype(np.uint64)
+    if spec.bit_reorder:
+        mant = (1 << spec.mantissa_bits) - 1
+        sign = 1 << spec.mantissa_bits
+        expm = ((1 << spec.exponent_bits) - 1) << (spec.mantissa_bits + 1)
+        w = (w & mant) | ((w >> spec.exponent_bits) & sign) | ((w << 1) & expm)
+    return w
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("numel", [0, 1, 7, (1 << 20) + 5, 3 << 20])
+def test_split_lanes_threaded_and_selected_only(dtype, numel):
+    """nz_split_lanes splits large inputs in 1 Mi-element blocks on the
+    host's threads and skips lanes whose buffer is NULL; every lane equals
+    the reorder restated in numpy."""
+    spec = DTYPES[dtype]
+    raw = (torch.randn(numel, generator=torch.Generator().manual_seed(numel)) * 0.02).to(dtype)
+    raw = raw.view(torch.uint8).numpy()
+    dt = _dtype_struct(spec)
+    words = _reordered_words(raw, spec)
+    lanes = _native.split_lanes(raw, dt)
+    for lane in range(spec.element_size):
+        assert np.array_equal(lanes[lane], ((words >> (8 * lane)) & 0xFF).astype(np.uint8))
+    only = _native.split_lanes(raw, dt, selected_only=True)
+    assert [lane is None for lane in only] == [k != spec.gpu_stream for k in range(spec.element_size)]
+    assert np.array_equal(only[spec.gpu_stream], lanes[spec.gpu_stream])
+
+
+def test_split_lanes_requires_the_selected_lane():
+    spec = DTYPES[torch.bfloat16]
+    raw = np.zeros(16, dtype=np.uint8)
+    lib = _native.load()
+    keep = np.empty(8, dtype=np.uint8)
+    lanes = (ctypes.c_void_p * 4)(keep.ctypes.data, None, None, None)  # lane 1 is bf16's selected lane
+    assert lib.nz_split_lanes(raw.ctypes.data, 8, ctypes.byref(_dtype_struct(spec)), lanes) != 0
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+def test_exponent_histograms_match_numpy(dtype):
+    """Per-chunk exponent-field histograms, counted on the host's threads,
+    with a ragged last chunk."""
+    spec = DTYPES[dtype]
+    numel = 5 * 131072 + 999
+    raw = (torch.randn(numel, generator=torch.Generator().manual_seed(3)) * 0.3).to(dtype).view(torch.uint8).numpy()
+    step = 131072
+    hist = np.asarray(_native.exponent_histograms(raw, _dtype_struct(spec), step)).reshape(-1, 256)
+    w = raw.view(np.uint16 if spec.element_size == 2 else np.uint32).astype(np.int64)
+    e = (w >> spec.mantissa_bits) & ((1 << spec.exponent_bits) - 1)
+    want = np.stack([np.bincount(e[s:s + step], minlength=256) for s in range(0, numel, step)])
+    assert np.array_equal(hist.astype(np.int64), want)
+
+
+@pytest.mark.parametrize("size", [0, 3, (1 << 22) - 1, (1 << 22) + 1, 3 * (1 << 22) + 17])
+def test_byte_counts_across_blocks(size):
+    """count_tokens without a pair vocabulary (4 Mi-byte blocks on the
+    host's threads) equals a plain byte count."""
+    data = np.random.default_rng(size).integers(0, 256, size, dtype=np.uint8)
+    counts = np.asarray(_native.count_tokens(data, b""))
+    assert np.array_equal(counts[:256].astype(np.int64), np.bincount(data, minlength=256))

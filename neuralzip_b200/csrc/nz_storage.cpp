@@ -123,23 +123,20 @@ uint64_t mixed_encode(const Codebook& cb, const uint8_t* data, uint64_t size, ui
     return cursor;
 }
 
-// Forward MSB-first window: 64 bits starting at bit `at` of `stream`
-// (`bytes` long), zeros past the end.
+// Forward MSB-first window starting at bit `at` of `stream` (`bytes`
+// long), zeros past the end. Codes are at most 56 bits, so one big-endian
+// 8-byte load shifted by at most 7 bits holds every bit a token can read
+// (the lowest `at & 7` bits of the window are left zero).
 static inline uint64_t forward_window(const uint8_t* stream, uint64_t bytes, uint64_t at) {
     const uint64_t byte = at >> 3;
     uint64_t w = 0;
-    if (byte + 9 <= bytes) {
-        for (int i = 0; i < 8; ++i) w = (w << 8) | stream[byte + i];
-        const uint32_t sh = at & 7U;
-        if (sh) w = (w << sh) | (static_cast<uint64_t>(stream[byte + 8]) >> (8 - sh));
-        return w;
+    if (byte + 8 <= bytes) {
+        std::memcpy(&w, stream + byte, 8);
+        w = __builtin_bswap64(w);
+    } else {
+        for (uint64_t i = 0; i < 8; ++i) w = (w << 8) | (byte + i < bytes ? stream[byte + i] : 0U);
     }
-    for (int i = 0; i < 9; ++i) {
-        const uint64_t b = byte + i < bytes ? stream[byte + i] : 0;
-        if (i < 8) w = (w << 8) | b;
-        else if (at & 7U) w = (w << (at & 7U)) | (b >> (8 - (at & 7U)));
-    }
-    return w;
+    return w << (at & 7U);
 }
 
 // One token from a 64-bit window: writes its bytes (<= 2) and returns its
@@ -170,31 +167,65 @@ void mixed_decode(const Codebook& cb, const uint8_t* data, uint64_t size, uint8_
         return static_cast<uint32_t>(p[0]) | (static_cast<uint32_t>(p[1]) << 8) |
                (static_cast<uint32_t>(p[2]) << 16) | (static_cast<uint32_t>(p[3]) << 24);
     };
-    uint64_t cursor = 32, written = 0;
-    for (unsigned lane = 0; lane < 4; ++lane) {
-        const uint32_t count = read_u32(data + 8 * lane);
-        const uint64_t bit_size = read_u32(data + 8 * lane + 4);
-        const uint64_t bytes = (bit_size + 7) / 8;
-        if (bytes > size - cursor || count > expected - written)
+    // The frame's four lanes are independent bitstreams: each is decoded
+    // into its own stretch of scratch (at most two bytes a token), the four
+    // in lockstep (four dependency chains instead of one), and the stretches
+    // are then copied out in lane order.
+    struct Lane {
+        const uint8_t* stream;
+        uint64_t bytes, bits, pos, tokens, written;
+        uint8_t* dst;
+    } lanes[4];
+    uint64_t cursor = 32, tokens_total = 0;
+    for (unsigned k = 0; k < 4; ++k) {
+        Lane& l = lanes[k];
+        l.tokens = read_u32(data + 8 * k);
+        l.bits = read_u32(data + 8 * k + 4);
+        l.bytes = (l.bits + 7) / 8;
+        if (l.bytes > size - cursor || l.tokens > expected - tokens_total)
             throw Error(NZ_EVALUE, "Mixed frame lengths exceed its payload.");
-        const uint8_t* stream = data + cursor;
-        uint64_t pos = 0;
-        for (uint32_t i = 0; i < count; ++i) {
-            uint32_t value = 0, n = 0;
-            const uint32_t length = decode_token(cb, forward_window(stream, bytes, pos), &value, &n);
-            if (!length) throw Error(NZ_EVALUE, "Invalid mixed Huffman prefix.");
-            if (pos + length > bit_size) throw Error(NZ_EVALUE, "Truncated mixed Huffman code.");
-            if (n > expected - written) throw Error(NZ_EVALUE, "Mixed expansion exceeds exponent count.");
-            out[written++] = static_cast<uint8_t>(value);
-            if (n == 2) out[written++] = static_cast<uint8_t>(value >> 8);
-            pos += length;
-        }
-        if (pos != bit_size) throw Error(NZ_EVALUE, "Mixed frame has unconsumed code bits.");
-        if (bit_size % 8 && (stream[bytes - 1] & ((1U << (8 - bit_size % 8)) - 1)))
-            throw Error(NZ_EVALUE, "Mixed frame has nonzero padding.");
-        cursor += bytes;
+        l.stream = data + cursor;
+        l.pos = l.written = 0;
+        tokens_total += l.tokens;
+        cursor += l.bytes;
     }
-    if (cursor != size || written != expected) throw Error(NZ_EVALUE, "Mixed decoded size mismatch.");
+    if (cursor != size) throw Error(NZ_EVALUE, "Mixed decoded size mismatch.");
+    thread_local std::vector<uint8_t> scratch;
+    if (scratch.size() < 2 * tokens_total) scratch.resize(2 * tokens_total);
+    uint64_t offset = 0;
+    for (Lane& l : lanes) {
+        l.dst = scratch.data() + offset;
+        offset += 2 * l.tokens;
+    }
+    auto token = [&](Lane& l) {
+        uint32_t value = 0, n = 0;
+        const uint32_t length = decode_token(cb, forward_window(l.stream, l.bytes, l.pos), &value, &n);
+        if (!length) throw Error(NZ_EVALUE, "Invalid mixed Huffman prefix.");
+        if (l.pos + length > l.bits) throw Error(NZ_EVALUE, "Truncated mixed Huffman code.");
+        l.dst[l.written] = static_cast<uint8_t>(value);
+        l.dst[l.written + 1] = static_cast<uint8_t>(value >> 8);
+        l.written += n;
+        l.pos += length;
+    };
+    uint64_t together = lanes[0].tokens;
+    for (const Lane& l : lanes) together = std::min(together, l.tokens);
+    for (uint64_t i = 0; i < together; ++i) {
+        token(lanes[0]);
+        token(lanes[1]);
+        token(lanes[2]);
+        token(lanes[3]);
+    }
+    uint64_t written = 0;
+    for (Lane& l : lanes) {
+        for (uint64_t i = together; i < l.tokens; ++i) token(l);
+        if (l.pos != l.bits) throw Error(NZ_EVALUE, "Mixed frame has unconsumed code bits.");
+        if (l.bits % 8 && (l.stream[l.bytes - 1] & ((1U << (8 - l.bits % 8)) - 1)))
+            throw Error(NZ_EVALUE, "Mixed frame has nonzero padding.");
+        if (l.written > expected - written) throw Error(NZ_EVALUE, "Mixed expansion exceeds exponent count.");
+        std::memcpy(out + written, l.dst, l.written);
+        written += l.written;
+    }
+    if (written != expected) throw Error(NZ_EVALUE, "Mixed decoded size mismatch.");
 }
 
 uint64_t huff0_encode(const Codebook& cb, const uint8_t* data, uint64_t size, uint8_t* out, uint64_t cap) {

@@ -409,3 +409,38 @@ def test_byte_counts_across_blocks(size):
     data = np.random.default_rng(size).integers(0, 256, size, dtype=np.uint8)
     counts = np.asarray(_native.count_tokens(data, b""))
     assert np.array_equal(counts[:256].astype(np.int64), np.bincount(data, minlength=256))
+
+
+@pytest.mark.parametrize("size", [1, 2, 3, 5, 4096 + 3, 131072])
+def test_mixed_decode_lockstep_round_trips(size):
+    """The host mixed decoder runs a frame's four lanes in lockstep; frames
+    of every size (including lanes with unequal token counts) decode back
+    to their bytes."""
+    raw = H.gaussian_raw(max(size, 64), 0.02, torch.bfloat16, size)
+    sel = H.selected_lane(raw, DTYPES[torch.bfloat16])[:size]
+    lengths, vocab = H.mixed_book_for(sel)
+    book = _native.NativeCodebook(lengths, None, vocab)
+    frame = _native.mixed_encode(book, sel, 4 * size + 64)
+    assert np.array_equal(_native.mixed_decode(book, frame, size), sel)
+
+
+def test_mixed_decode_rejects_corrupt_frames():
+    raw = H.gaussian_raw(20000, 0.02, torch.bfloat16, 9)
+    sel = H.selected_lane(raw, DTYPES[torch.bfloat16])
+    lengths, vocab = H.mixed_book_for(sel)
+    book = _native.NativeCodebook(lengths, None, vocab)
+    frame = bytearray(_native.mixed_encode(book, sel, 4 * len(sel) + 64))
+    n = len(sel)
+    cases = {
+        "truncated": bytes(frame[:-1]),
+        "trailing byte": bytes(frame) + b"\0",
+        "token count + 1": (int.from_bytes(frame[:4], "little") + 1).to_bytes(4, "little") + bytes(frame[4:]),
+        "bit count - 1": bytes(frame[:4]) + (int.from_bytes(frame[4:8], "little") - 1).to_bytes(4, "little") + bytes(frame[8:]),
+        "short header": bytes(frame[:31]),
+    }
+    for what, bad in cases.items():
+        with pytest.raises(ValueError):
+            _native.mixed_decode(book, bad, n)
+            pytest.fail(what)
+    with pytest.raises(ValueError):  # one byte more expected than the frame holds
+        _native.mixed_decode(book, bytes(frame), n + 1)

@@ -258,27 +258,76 @@ uint64_t huff0_encode(const Codebook& cb, const uint8_t* data, uint64_t size, ui
     return total;
 }
 
-// Backward reader: `top` counts the unread bits below the end marker; the
-// next bits to read are [top - n, top) with bit top - 1 read first.
-static inline uint32_t backward_peek12(const uint8_t* stream, uint64_t size, int64_t top) {
-    // Fast path: one unaligned little-endian 8-byte load starting at the
-    // byte that holds bit top - 12 (the window's lowest bit).
-    if (top >= 12) {
-        const uint64_t first = static_cast<uint64_t>(top - 12) >> 3;
-        if (first + 8 <= size) {
-            uint64_t word;
-            std::memcpy(&word, stream + first, 8);
-            return static_cast<uint32_t>((word >> ((top - 12) & 7)) & 0xFFFU);
+// Blocks of four symbols of each of the four streams of a Huff0 block,
+// from position k: every block reloads each stream's 64-bit container (at
+// least 57 of its next bits, left-aligned; zeros below the stream's start)
+// and decodes four symbols of at most 12 bits from it. The state lives in
+// scalars (stores to the output bytes may alias anything else), and each
+// stream's bits used by the call go to used[], for the caller to check
+// against the `top` unread bits the streams held when the call started.
+static inline __attribute__((always_inline)) void huff0_blocks_body(
+    const uint32_t* single, const uint8_t* const* stream, const uint64_t* sizes, const int64_t* top,
+    uint8_t* const* dst, uint64_t k, uint64_t run, uint64_t* used, uint32_t* bad) {
+    auto load = [&](int s, uint64_t u) {
+        const int64_t t = top[s] - static_cast<int64_t>(u);
+        if (t <= 0) return uint64_t{0};
+        const uint64_t last = static_cast<uint64_t>((t + 7) >> 3);
+        const uint64_t start = last >= 8 ? last - 8 : 0;
+        uint64_t w = 0;
+        if (start + 8 <= sizes[s]) {
+            std::memcpy(&w, stream[s] + start, 8);
+        } else {
+            for (uint64_t b = last; b-- > start;) w = (w << 8) | stream[s][b];
+        }
+        const int64_t have = t - static_cast<int64_t>(8 * start);
+        return have >= 64 ? w : w << (64 - have);
+    };
+    uint64_t u0 = 0, u1 = 0, u2 = 0, u3 = 0;
+    uint32_t invalid = 0;
+    uint8_t* o0 = dst[0] + k;
+    uint8_t* o1 = dst[1] + k;
+    uint8_t* o2 = dst[2] + k;
+    uint8_t* o3 = dst[3] + k;
+    for (uint64_t r = 0; r < run; ++r) {
+        uint64_t c0 = load(0, u0), c1 = load(1, u1), c2 = load(2, u2), c3 = load(3, u3);
+        for (int j = 0; j < 4; ++j) {
+            const uint32_t e0 = single[c0 >> 52], e1 = single[c1 >> 52];
+            const uint32_t e2 = single[c2 >> 52], e3 = single[c3 >> 52];
+            invalid |= ((e0 >> 16) & 3U) == 0 || ((e1 >> 16) & 3U) == 0 || ((e2 >> 16) & 3U) == 0 ||
+                       ((e3 >> 16) & 3U) == 0;
+            const uint32_t l0 = e0 >> 20, l1 = e1 >> 20, l2 = e2 >> 20, l3 = e3 >> 20;
+            o0[4 * r + j] = static_cast<uint8_t>(e0);
+            o1[4 * r + j] = static_cast<uint8_t>(e1);
+            o2[4 * r + j] = static_cast<uint8_t>(e2);
+            o3[4 * r + j] = static_cast<uint8_t>(e3);
+            c0 <<= l0, c1 <<= l1, c2 <<= l2, c3 <<= l3;
+            u0 += l0, u1 += l1, u2 += l2, u3 += l3;
         }
     }
-    // Little-endian 64-bit word covering bits [8 * b0, 8 * b0 + 64).
-    const int64_t b0 = top >= 64 ? (top - 64 + 7) / 8 : 0;
-    uint64_t w = 0;
-    const int64_t last = (top + 7) / 8;  // bytes that hold unread bits
-    for (int64_t b = last - 1; b >= b0; --b) w = (w << 8) | stream[b];
-    const int64_t shift = top - 12 - 8 * b0;
-    if (shift >= 0) return static_cast<uint32_t>((w >> shift) & 0xFFFU);
-    return static_cast<uint32_t>((w << (-shift)) & 0xFFFU);
+    used[0] = u0, used[1] = u1, used[2] = u2, used[3] = u3;
+    *bad |= invalid;
+}
+
+static void huff0_blocks_generic(const uint32_t* single, const uint8_t* const* stream, const uint64_t* sizes,
+                                 const int64_t* top, uint8_t* const* dst, uint64_t k, uint64_t run, uint64_t* used,
+                                 uint32_t* bad) {
+    huff0_blocks_body(single, stream, sizes, top, dst, k, run, used, bad);
+}
+
+// The same with BMI2's shifts by any register (no round trip through CL).
+__attribute__((target("bmi2"))) static void huff0_blocks_bmi2(const uint32_t* single, const uint8_t* const* stream,
+                                                              const uint64_t* sizes, const int64_t* top,
+                                                              uint8_t* const* dst, uint64_t k, uint64_t run,
+                                                              uint64_t* used, uint32_t* bad) {
+    huff0_blocks_body(single, stream, sizes, top, dst, k, run, used, bad);
+}
+
+static void huff0_blocks(const uint32_t* single, const uint8_t* const* stream, const uint64_t* sizes,
+                         const int64_t* top, uint8_t* const* dst, uint64_t k, uint64_t run, uint64_t* used,
+                         uint32_t* bad) {
+    static const bool bmi2 = __builtin_cpu_supports("bmi2");
+    if (bmi2) huff0_blocks_bmi2(single, stream, sizes, top, dst, k, run, used, bad);
+    else huff0_blocks_generic(single, stream, sizes, top, dst, k, run, used, bad);
 }
 
 void huff0_decode(const Codebook& cb, const uint8_t* data, uint64_t size, uint8_t* out, uint64_t count) {
@@ -305,28 +354,60 @@ void huff0_decode(const Codebook& cb, const uint8_t* data, uint64_t size, uint8_
         end[s] = s == 3 ? count : std::min<uint64_t>(count, segment * (s + 1));
         at += n;
     }
-    // The four streams are independent: decode them in lockstep, one symbol
-    // of each per step (four dependency chains instead of one), and check
-    // the entries once at the end of the run.
+    // The four streams are independent: decode them in lockstep (four
+    // dependency chains instead of one) by huff0_blocks, then each stream's
+    // last few symbols one at a time from a freshly loaded container.
     const uint32_t* single = cb.single.data();
     uint32_t bad = 0;
+    uint64_t c[4];
+    auto reload = [&](int s) {
+        const int64_t t = top[s];
+        if (t <= 0) {
+            c[s] = 0;
+            return;
+        }
+        const uint64_t last = static_cast<uint64_t>((t + 7) >> 3);  // bytes that hold unread bits
+        const uint64_t start = last >= 8 ? last - 8 : 0;
+        uint64_t w = 0;
+        if (start + 8 <= sizes[s]) {
+            std::memcpy(&w, stream[s] + start, 8);
+        } else {
+            for (uint64_t b = last; b-- > start;) w = (w << 8) | stream[s][b];
+        }
+        const int64_t have = t - static_cast<int64_t>(8 * start);  // valid low bits of w
+        c[s] = have >= 64 ? w : w << (64 - have);
+    };
     auto step = [&](int s, uint64_t i) {
-        const uint32_t e = single[backward_peek12(stream[s], sizes[s], top[s])];
+        const uint32_t e = single[c[s] >> 52];
         const uint32_t length = e >> 20;
         bad |= static_cast<uint32_t>(!((e >> 16) & 3U)) | static_cast<uint32_t>(top[s] < static_cast<int64_t>(length));
         out[i] = static_cast<uint8_t>(e);
+        c[s] <<= length;
         top[s] -= length;
     };
     uint64_t together = end[3] - begin[3];
     for (int s = 0; s < 3; ++s) together = std::min(together, end[s] - begin[s]);
-    for (uint64_t k = 0; k < together && !bad; ++k) {
-        step(0, begin[0] + k);
-        step(1, begin[1] + k);
-        step(2, begin[2] + k);
-        step(3, begin[3] + k);
+    uint64_t k = 0;
+    uint8_t* dst[4] = {out + begin[0], out + begin[1], out + begin[2], out + begin[3]};
+    const uint64_t blocks = together / 4;
+    for (uint64_t done = 0; done < blocks && !bad;) {
+        // Up to 64 blocks of four symbols a stream between checks of the
+        // bits used against the bits the streams held.
+        const uint64_t run = std::min<uint64_t>(64, blocks - done);
+        uint64_t used[4];
+        huff0_blocks(single, stream, sizes, top, dst, k, run, used, &bad);
+        for (int s = 0; s < 4; ++s) {
+            top[s] -= static_cast<int64_t>(used[s]);
+            bad |= static_cast<uint32_t>(top[s] < 0);
+        }
+        k += 4 * run;
+        done += run;
     }
     for (int s = 0; s < 4 && !bad; ++s)
-        for (uint64_t i = begin[s] + together; i < end[s] && !bad; ++i) step(s, i);
+        for (uint64_t i = begin[s] + k; i < end[s] && !bad; ++i) {
+            reload(s);
+            step(s, i);
+        }
     if (bad) throw Error(NZ_EVALUE, "Corrupt Huff0 stream.");
     for (int s = 0; s < 4; ++s)
         if (top[s] != 0) throw Error(NZ_EVALUE, "Huff0 stream has unconsumed bits.");

@@ -325,7 +325,7 @@ __attribute__((target("bmi2"))) static void huff0_blocks_bmi2(const uint32_t* si
 static void huff0_blocks(const uint32_t* single, const uint8_t* const* stream, const uint64_t* sizes,
                          const int64_t* top, uint8_t* const* dst, uint64_t k, uint64_t run, uint64_t* used,
                          uint32_t* bad) {
-    static const bool bmi2 = __builtin_cpu_supports("bmi2");
+    static const bool bmi2 = (__builtin_cpu_init(), __builtin_cpu_supports("bmi2") != 0);
     if (bmi2) huff0_blocks_bmi2(single, stream, sizes, top, dst, k, run, used, bad);
     else huff0_blocks_generic(single, stream, sizes, top, dst, k, run, used, bad);
 }

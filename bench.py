@@ -1314,7 +1314,7 @@ def main():
                     "note": "one GPU's share of the multi-GPU workload (what each rank decodes under torchrun)"}
             if not args.no_generation:
                 log("generation: config3")
-                record, *_ = generation_record("config3", device, v3=True)
+                record, *_ = generation_record("config3", device, v3=True, graphs=True)
                 extras["generation"] = record
         else:
             m = config5a_record(args, world, rank, device, clocks, host_threads, args.layers_per_gpu)
